@@ -1,0 +1,135 @@
+/*
+ * ragged_b200.h -- C ABI of the B200 (sm_100a) segmented sum / max / softmax
+ * library, libragged_b200.so.
+ *
+ * It replaces the reference's native launcher (simon-jd/ragged-mlir):
+ * the nanobind module `ragged._native.DriverModule` declared in
+ * runtime/Driver.h:21-54 and bound in runtime/bindings.cpp:11-36, which
+ * loaded MLIR-generated cubins and ran manifest-described launch plans.
+ * Here the kernels are built into the library, so the ABI takes the problem
+ * (op, dtypes, D, N, B) and plain device pointers instead of a cubin and
+ * memref descriptors.  No C++ exception crosses it: every entry point
+ * returns an rg_status (0 = success) and rg_last_error() explains failures.
+ *
+ * Tensor contract (the reference's docs/abi.md and runtime.py:304-365):
+ *   values  [N, D] row-major, f32 or bf16, device memory
+ *   offsets [B + 1] i32 or i64, offsets[0] = 0, nondecreasing, offsets[B] = N
+ *   out     [B, D] for sum / max, [N, D] for softmax, same dtype as values,
+ *           disjoint from values and offsets
+ * All launches are asynchronous on the caller's stream; nothing is read back
+ * and nothing synchronises (the reference's "validated" mode).
+ */
+#ifndef RAGGED_B200_H
+#define RAGGED_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is
+ * exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ------------------------------------------------------------- constants */
+enum rg_status {
+  RG_OK = 0,
+  RG_ERR_INVALID_ARGUMENT = 1, /* shape, dtype, pointer or alignment problem  */
+  RG_ERR_UNSUPPORTED = 2,      /* valid request this build does not implement */
+  RG_ERR_WORKSPACE = 3,        /* workspace missing, misaligned or too small  */
+  RG_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed        */
+  RG_ERR_DEVICE = 5            /* no device, or not compute capability 10.0   */
+};
+
+enum rg_op { RG_OP_SUM = 0, RG_OP_MAX = 1, RG_OP_SOFTMAX = 2 };
+enum rg_dtype { RG_DTYPE_F32 = 0, RG_DTYPE_BF16 = 1 };
+enum rg_index { RG_INDEX_I32 = 0, RG_INDEX_I64 = 1 };
+
+/* Schedules.  CLASSIFIED and NAIVE are the reference's two strategies
+ * (python/ragged/runtime.py:252-268); ROWBALANCED is this build's
+ * row-balanced (merge-path) schedule for sum and max. */
+enum rg_schedule {
+  RG_SCHEDULE_CLASSIFIED = 0,
+  RG_SCHEDULE_NAIVE = 1,
+  RG_SCHEDULE_ROWBALANCED = 2
+};
+
+/* rg_run flags */
+#define RG_FLAG_NO_VECTORIZE 1u /* one feature per thread (reference Optimizations(vectorize=False)) */
+
+#define RG_MAX_LAUNCHES 8
+
+/* What one call launched (the reference's ExecutionReport grid / kernel
+ * fields, python/ragged/model.py:215-252). */
+typedef struct rg_report {
+  int32_t schedule;                       /* rg_schedule that ran             */
+  int32_t num_launches;                   /* kernel launches                  */
+  int32_t kernel_ids[RG_MAX_LAUNCHES];    /* see rg_kernel_name()             */
+  int32_t grid[RG_MAX_LAUNCHES][3];
+  int32_t block[RG_MAX_LAUNCHES];
+  int32_t shared_bytes[RG_MAX_LAUNCHES];
+  int32_t memsets;                        /* cudaMemsetAsync calls            */
+  int32_t d_vector;                       /* adjacent features per thread     */
+  int32_t d_tile;                         /* threads spanning one row tile    */
+  int32_t streams;                        /* streams used (1: caller's only)  */
+  int64_t workspace_bytes;                /* scratch the call required        */
+} rg_report;
+
+typedef struct rg_device_info {
+  int32_t device;
+  int32_t sm_count;
+  int32_t cc_major, cc_minor;
+  int64_t l2_bytes;
+  int32_t smem_per_block_optin;
+  int32_t max_threads_per_sm;
+} rg_device_info;
+
+/* ----------------------------------------------------------- entry points */
+
+/* Library version string, e.g. "ragged-b200 0.1.0 (sm_100a)". */
+const char *rg_version(void);
+
+/* Static description of a status code. */
+const char *rg_error_string(int status);
+
+/* Detail of the last failure on the calling thread ("" if none).  Replaces
+ * the reference's std::runtime_error text (runtime/Driver.cpp:85-95). */
+const char *rg_last_error(void);
+
+/* Properties of CUDA device `device`, queried once and cached.  Replaces
+ * the reference's device() / residentBlocks() helpers (Driver.h:34-37) and
+ * the L2 query of runtime.py:165-178. */
+int rg_get_device_info(int device, rg_device_info *info);
+
+/* Scratch bytes rg_run needs for this problem on the current device (0 for
+ * the block-per-segment schedule).  Replaces the workspace sizing of the
+ * reference's layout.py:186-243 (resolve_layout) and runtime.py:534-542. */
+int rg_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
+                       int schedule, int64_t max_len, int64_t *bytes);
+
+/* Launch one segmented operation on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream).  `workspace` must hold rg_workspace_bytes() bytes
+ * (256-byte aligned) and may be NULL when that is 0.  `max_len` is the
+ * caller's bound on the longest segment or -1 when unknown.  `report` may be
+ * NULL.  Replaces DriverModule.launch / add_plan / run_plan
+ * (runtime/Driver.h:31-47, runtime/Driver.cpp:247-353). */
+int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
+           const void *values, const void *offsets, void *out, void *workspace,
+           int64_t workspace_bytes, int schedule, int64_t max_len, uint32_t flags,
+           void *stream, rg_report *report);
+
+/* Name of a kernel id reported in rg_report.kernel_ids ("" if unknown). */
+const char *rg_kernel_name(int kernel_id);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RAGGED_B200_H */

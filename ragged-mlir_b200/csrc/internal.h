@@ -1,0 +1,70 @@
+// Host-side types shared by the launcher and the per-schedule launch code.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/ragged_b200.h"
+
+namespace rgb {
+
+struct Problem {
+  int op, dtype, index_dtype;
+  int64_t d, n, b;
+  const void *values;
+  const void *offsets;
+  void *out;
+  int64_t max_len;  // -1: unknown
+  uint32_t flags;
+};
+
+// Thread geometry: VEC adjacent features per thread (16-byte vectors where D
+// and the base addresses allow, the reference's d_vector rule of
+// python/ragged/optimizations.py:41-56), C = D / VEC vector columns,
+// G = 2^g_shift = min(32, pow2ceil(C)) lanes per row (the reference's
+// d_tile), and ceil(C / 32) column tiles.
+struct Geometry {
+  int vec;
+  int g_shift;
+  int vec_cols;
+  int col_tiles;
+};
+
+struct DeviceProps {
+  int device;
+  int sm_count;
+  int cc_major, cc_minor;
+  int64_t l2_bytes;
+  int smem_optin;
+  int max_threads_per_sm;
+};
+
+// Kernel ids reported through rg_report (names in launcher.cu).
+enum KernelId : int {
+  K_NAIVE = 1,
+  K_CLASSIFY = 2,
+  K_WORKER = 3,
+  K_SPLIT_NORMALIZE = 4,
+  K_ROWBAL = 5,
+  K_ROWBAL_FIXUP = 6,
+  K_SHARD_COMBINE = 7,
+};
+
+// Recording helper for rg_report.
+void record_launch(rg_report *report, int kernel_id, dim3 grid, int block, int shared_bytes);
+
+// Thread-local error detail.
+int fail(int status, const std::string &message);
+int check_cuda(cudaError_t err, const char *what);
+
+int elem_bytes(int dtype);
+Geometry make_geometry(const Problem &p);
+int device_props(DeviceProps *props);  // current device
+
+// Per-schedule entry points (launch on stream, record into report).
+int launch_naive(const Problem &p, const Geometry &g, cudaStream_t stream, rg_report *report);
+
+}  // namespace rgb

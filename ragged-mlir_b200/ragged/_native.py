@@ -1,0 +1,135 @@
+"""ctypes binding of libragged_b200.so (C ABI: include/ragged_b200.h).
+
+Replaces the reference's nanobind module ``ragged._native`` (runtime/
+bindings.cpp:11-36).  The library is loaded lazily on first use; if it is
+missing, ``RuntimeUnavailable`` is raised -- there is no fallback path.
+Status codes map onto the reference's exceptions: invalid arguments raise
+``ValidationError``, a missing or unsupported device ``RuntimeUnavailable``,
+and CUDA failures ``RuntimeError`` carrying the CUDA error name and text
+(as runtime/Driver.cpp:85-95 did).
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+import threading
+
+from .errors import RuntimeUnavailable, ValidationError
+
+LIBRARY = Path(__file__).resolve().parent / "_lib" / "libragged_b200.so"
+
+RG_OK, RG_ERR_INVALID_ARGUMENT, RG_ERR_UNSUPPORTED, RG_ERR_WORKSPACE, RG_ERR_CUDA, RG_ERR_DEVICE = range(6)
+OPS = {"sum": 0, "max": 1, "softmax": 2}
+DTYPES = {"f32": 0, "bf16": 1}
+INDEX = {"i32": 0, "i64": 1}
+SCHEDULES = {"classified": 0, "naive": 1, "rowbalanced": 2}
+SCHEDULE_NAMES = {value: key for key, value in SCHEDULES.items()}
+FLAG_NO_VECTORIZE = 1
+MAX_LAUNCHES = 8
+
+# Every symbol include/ragged_b200.h declares.
+EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
+            "rg_run", "rg_kernel_name")
+
+
+class Report(ctypes.Structure):
+    _fields_ = [("schedule", ctypes.c_int32), ("num_launches", ctypes.c_int32),
+                ("kernel_ids", ctypes.c_int32 * MAX_LAUNCHES), ("grid", (ctypes.c_int32 * 3) * MAX_LAUNCHES),
+                ("block", ctypes.c_int32 * MAX_LAUNCHES), ("shared_bytes", ctypes.c_int32 * MAX_LAUNCHES),
+                ("memsets", ctypes.c_int32), ("d_vector", ctypes.c_int32), ("d_tile", ctypes.c_int32),
+                ("streams", ctypes.c_int32), ("workspace_bytes", ctypes.c_int64)]
+
+
+class DeviceInfo(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("sm_count", ctypes.c_int32), ("cc_major", ctypes.c_int32),
+                ("cc_minor", ctypes.c_int32), ("l2_bytes", ctypes.c_int64),
+                ("smem_per_block_optin", ctypes.c_int32), ("max_threads_per_sm", ctypes.c_int32)]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def library(path: Path | None = None):
+    """The loaded library (raises RuntimeUnavailable when it is missing)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        target = Path(path) if path is not None else LIBRARY
+        if not target.exists():
+            raise RuntimeUnavailable(f"native library {target} is missing; build it with "
+                                     "`python ragged-mlir_b200/build.py` (no CPU fallback exists)")
+        try:
+            lib = ctypes.CDLL(str(target))
+        except OSError as exc:
+            raise RuntimeUnavailable(f"cannot load {target}: {exc}") from exc
+        i32, i64, p, u32 = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32
+        lib.rg_version.restype = ctypes.c_char_p
+        lib.rg_error_string.restype = ctypes.c_char_p
+        lib.rg_error_string.argtypes = [i32]
+        lib.rg_last_error.restype = ctypes.c_char_p
+        lib.rg_kernel_name.restype = ctypes.c_char_p
+        lib.rg_kernel_name.argtypes = [i32]
+        lib.rg_get_device_info.argtypes = [i32, ctypes.POINTER(DeviceInfo)]
+        lib.rg_get_device_info.restype = i32
+        lib.rg_workspace_bytes.argtypes = [i32, i32, i32, i64, i64, i64, i32, i64, ctypes.POINTER(i64)]
+        lib.rg_workspace_bytes.restype = i32
+        lib.rg_run.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, p, i64, i32, i64, u32, p,
+                               ctypes.POINTER(Report)]
+        lib.rg_run.restype = i32
+        _lib = lib
+        return lib
+
+
+def raise_for(status: int, what: str) -> None:
+    if status == RG_OK:
+        return
+    lib = library()
+    detail = lib.rg_last_error().decode(errors="replace")
+    message = f"{what}: {lib.rg_error_string(status).decode()}: {detail}"
+    if status in (RG_ERR_INVALID_ARGUMENT, RG_ERR_WORKSPACE):
+        raise ValidationError(message)
+    if status in (RG_ERR_DEVICE, RG_ERR_UNSUPPORTED):
+        raise RuntimeUnavailable(message)
+    raise RuntimeError(message)
+
+
+def version() -> str:
+    return library().rg_version().decode()
+
+
+def kernel_name(kernel_id: int) -> str:
+    return library().rg_kernel_name(kernel_id).decode()
+
+
+_device_info: dict[int, DeviceInfo] = {}
+
+
+def device_info(device: int) -> DeviceInfo:
+    info = _device_info.get(device)
+    if info is None:
+        info = DeviceInfo()
+        raise_for(library().rg_get_device_info(device, ctypes.byref(info)), "rg_get_device_info")
+        _device_info[device] = info
+    return info
+
+
+def workspace_bytes(op: str, dtype: str, index: str, d: int, n: int, b: int, schedule: str,
+                    max_len: int | None) -> int:
+    out = ctypes.c_int64(0)
+    raise_for(library().rg_workspace_bytes(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, SCHEDULES[schedule],
+                                           -1 if max_len is None else max_len, ctypes.byref(out)),
+              "rg_workspace_bytes")
+    return int(out.value)
+
+
+def run(op: str, dtype: str, index: str, d: int, n: int, b: int, values_ptr: int, offsets_ptr: int,
+        out_ptr: int, workspace_ptr: int, workspace_bytes: int, schedule: str, max_len: int | None,
+        flags: int, stream: int) -> Report:
+    report = Report()
+    status = library().rg_run(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, values_ptr, offsets_ptr, out_ptr,
+                              workspace_ptr or None, workspace_bytes, SCHEDULES[schedule],
+                              -1 if max_len is None else max_len, flags, stream or None, ctypes.byref(report))
+    raise_for(status, "rg_run")
+    return report

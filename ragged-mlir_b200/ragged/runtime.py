@@ -1,0 +1,240 @@
+"""``CompiledProgram.run``: validate, choose a schedule, launch on a stream.
+
+Mirrors the reference's python/ragged/runtime.py (CompiledProgram 218-558):
+the same signature ``run(values, offsets, out, stream=None,
+mode="validated", *, debug_buffers=None, mask=None, concurrent=True,
+select="auto", max_len=None) -> ExecutionReport``, the same tensor checks
+and error classes (runtime.py:304-365), scratch allocated from PyTorch's
+caching allocator on the execution stream (runtime.py:534-545), no device
+readback and no synchronisation.  Below it there is no module loading or
+launch-plan machinery: one call into libragged_b200.so (``rg_run``) chooses
+grids, relocates scratch and launches the sm_100a kernels on the stream.
+"""
+from __future__ import annotations
+
+from contextlib import nullcontext
+from dataclasses import replace
+import importlib
+import threading
+import time
+from typing import Any
+
+from . import _native
+from .cache import Artifact
+from .errors import CacheMismatch, RuntimeUnavailable, ValidationError
+from .model import ExecutionReport, ProgramSpec, runs_on
+from .selection import default_model
+
+I64_MAX = 2**63 - 1
+# Segment-length class bounds of the classified schedule (warp <= 32 rows,
+# CTA <= 4096 rows, longer ones split), as in the reference's Passes.cpp:17-18.
+THRESHOLDS = (32, 4096)
+
+_lock = threading.RLock()
+_checked_devices: set[int] = set()
+_device_l2_mib: dict[int, float | None] = {}
+
+
+def _torch():
+    try:
+        return importlib.import_module("torch")
+    except ImportError as exc:
+        raise RuntimeUnavailable("PyTorch is not installed; install the GPU environment to execute") from exc
+
+
+def device_l2_mib(values) -> float | None:
+    """L2 capacity (MiB) of the CUDA device holding ``values``, cached."""
+    device = getattr(values, "device", None)
+    if getattr(device, "type", None) != "cuda":
+        return None
+    index = device.index if device.index is not None else 0
+    if index not in _device_l2_mib:
+        try:
+            l2 = _native.device_info(index).l2_bytes
+        except Exception:  # noqa: BLE001 - no library/device: the model's own L2 is used
+            l2 = 0
+        _device_l2_mib[index] = l2 / 2**20 if l2 > 0 else None
+    return _device_l2_mib[index]
+
+
+def _overlaps(left: Any, right: Any) -> bool:
+    lstart, rstart = left.data_ptr(), right.data_ptr()
+    lend = lstart + left.numel() * left.element_size()
+    rend = rstart + right.numel() * right.element_size()
+    return lstart < rend and rstart < lend
+
+
+class CompiledProgram:
+    def __init__(self, spec: ProgramSpec, artifact: Artifact, *, cache_hit: bool = False,
+                 naive: "CompiledProgram | None" = None):
+        if not isinstance(spec, ProgramSpec):
+            raise ValidationError("spec must be a ProgramSpec")
+        if artifact.key.ir_hash != spec.ir_hash:
+            raise CacheMismatch("artifact was recorded for a different specialization")
+        self.spec, self.artifact, self.cache_hit = spec, artifact, cache_hit
+        self._schedules = tuple(artifact.metadata.get("schedules", ("naive",)))
+        self._digest = artifact.key.digest
+        self._selects = spec.strategy == "auto" and "naive" not in self._schedules
+        if naive is not None and (not self._selects or naive.spec != replace(spec, strategy="naive")):
+            raise CacheMismatch("a block-per-segment companion must be the naive strategy of a classifying program")
+        self.naive = naive
+        self._choices: dict[tuple, tuple[str, dict[str, Any]]] = {}
+        self._workspace: dict[tuple, int] = {}
+        tile, vec = spec.optimizations.geometry(spec.feature_dim, spec.dtype)
+        self._span = tile * vec
+        self._flags = 0 if spec.optimizations.vectorize else _native.FLAG_NO_VECTORIZE
+
+    @property
+    def selects(self) -> bool:
+        """Whether this program chooses among schedules per call."""
+        return self._selects
+
+    @property
+    def schedules(self) -> tuple[str, ...]:
+        return self._schedules + (("naive",) if self.naive is not None else ())
+
+    def choose(self, n: int, b: int, max_len: int | None, l2_mib: float | None = None) -> tuple[str, dict[str, Any]]:
+        """The schedule ``run(select="auto")`` uses and why."""
+        if not self._selects:
+            return self._schedules[0], {}
+        key = (n, b, max_len, l2_mib)
+        choice = self._choices.get(key)
+        if choice is None:
+            if len(self._choices) >= 256:
+                self._choices.clear()
+            element = 2 if self.spec.dtype == "bf16" else 4
+            choice = self._choices[key] = default_model().choose(
+                self.spec.op, n, b, self.spec.feature_dim, max_len, self._span, element, l2_mib=l2_mib,
+                available=self.schedules)
+        return choice
+
+    def close(self) -> None:
+        """Nothing to unload: kernels live in the shared library."""
+
+    def _validate_tensors(self, values, offsets, out, torch) -> tuple[int, int]:
+        for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
+            if not isinstance(tensor, torch.Tensor):
+                raise ValidationError(f"{name} must be a torch.Tensor")
+            if not tensor.is_cuda:
+                raise RuntimeUnavailable(f"{name} must be on a CUDA device that runs {self.spec.chip} code; "
+                                         "no CPU execution fallback exists")
+            if not tensor.is_contiguous():
+                raise ValidationError(f"{name} must be row-major contiguous")
+            if tensor.requires_grad:
+                raise ValidationError("autograd is outside the supported forward-only contract")
+        if values.device != offsets.device or values.device != out.device:
+            raise ValidationError("values, offsets and out must use the same CUDA device")
+        if values.ndim != 2 or values.shape[1] != self.spec.feature_dim:
+            raise ValidationError("values must have shape [N, static D]")
+        if offsets.ndim != 1 or offsets.numel() < 1:
+            raise ValidationError("offsets must have shape [B+1], including [0] when B=0")
+        dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype]
+        offset_dtype = {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype]
+        if values.dtype != dtype or out.dtype != dtype or offsets.dtype != offset_dtype:
+            raise ValidationError("tensor dtype differs from compiled dtype/offsets specialization")
+        _, vector = self.spec.optimizations.geometry(self.spec.feature_dim, self.spec.dtype)
+        if vector > 1:
+            for name, tensor in (("values", values), ("out", out)):
+                if tensor.numel():
+                    need = vector * tensor.element_size()
+                    if tensor.data_ptr() % need:
+                        raise ValidationError(f"{name} must be {need}-byte aligned: this specialization accesses "
+                                              f"{vector} features at a time (compile with vectorize=False for "
+                                              "unaligned views)")
+        n, b = values.shape[0], offsets.numel() - 1
+        if b == 0 and n != 0:
+            raise ValidationError("B=0 requires N=0; values cannot exist without segments")
+        if self.spec.offsets_dtype == "i32" and n > 2**31 - 1:
+            raise ValidationError("N exceeds the i32 offsets range")
+        expected = (n if self.spec.op == "softmax" else b, self.spec.feature_dim)
+        if tuple(out.shape) != expected:
+            raise ValidationError(f"out shape must be {expected}")
+        if _overlaps(offsets, values) or _overlaps(offsets, out):
+            raise ValidationError("offsets must not alias values or out")
+        if _overlaps(values, out):
+            raise ValidationError("out aliases values without a compiler-proven safe in-place schedule")
+        return n, b
+
+    def workspace_bytes(self, n: int, b: int, schedule: str, max_len: int | None = None) -> int:
+        key = (n, b, schedule, max_len)
+        nbytes = self._workspace.get(key)
+        if nbytes is None:
+            if len(self._workspace) >= 256:
+                self._workspace.clear()
+            nbytes = self._workspace[key] = _native.workspace_bytes(
+                self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b, schedule, max_len)
+        return nbytes
+
+    def run(self, values, offsets, out, stream=None, mode: str = "validated", *,
+            debug_buffers: dict[str, Any] | None = None, mask=None, concurrent: bool = True,
+            select: str = "auto", max_len: int | None = None) -> ExecutionReport:
+        """Launch on ``stream`` (default: the current stream of the values'
+        device).  Validated mode reads nothing back and never synchronises.
+        ``select`` is "auto" (cost model; ``max_len`` is the caller's bound on
+        the longest segment, a wrong value costs time, never correctness), or
+        forces "classified", "naive" or "rowbalanced"."""
+        if select not in ("auto", "classified", "naive", "rowbalanced"):
+            raise ValidationError("select must be auto, classified, naive or rowbalanced")
+        if max_len is not None and (type(max_len) is not int or max_len < 0):
+            raise ValidationError("max_len must be None or a nonnegative int")
+        if mode not in ("validated", "checked"):
+            raise ValidationError("mode must be validated or checked")
+        if mode == "checked":
+            raise RuntimeUnavailable("checked execution (device offsets validation) is not implemented by "
+                                     "libragged_b200; use validated mode with valid offsets")
+        if (mask is not None) != self.spec.mask:
+            raise ValidationError("mask presence must match the compiled specialization")
+        if debug_buffers is not None:
+            raise ValidationError("debug_buffers requires an empty dict and a debug_visits specialization")
+        if select != "auto" and select not in self.schedules:
+            raise ValidationError(f"select={select} is not a schedule of this program ({', '.join(self.schedules)})")
+        torch = _torch()
+        n, b = self._validate_tensors(values, offsets, out, torch)
+        started = time.perf_counter()
+        if select == "auto":
+            schedule, selection = self.choose(n, b, max_len, device_l2_mib(values))
+        else:
+            schedule, selection = select, {"forced": True}
+        if b == 0:
+            return self._report(schedule, selection, started, None, 0)
+        with torch.cuda.device(values.device):
+            ordinal = values.device.index
+            if ordinal not in _checked_devices:
+                capability = tuple(torch.cuda.get_device_capability(values.device))
+                if not runs_on(self.spec.chip, capability):
+                    raise RuntimeUnavailable(f"compiled target {self.spec.chip} does not run on the current device "
+                                             f"(sm_{capability[0]}{capability[1]})")
+                _checked_devices.add(ordinal)
+            active = stream if stream is not None else torch.cuda.current_stream(values.device)
+            if not isinstance(active, torch.cuda.Stream) or active.device != values.device:
+                raise ValidationError("stream must be a torch.cuda.Stream on the values device")
+            nbytes = self.workspace_bytes(n, b, schedule, max_len)
+            scratch, base = None, 0
+            if nbytes:
+                # Scratch comes from the caching allocator ON the execution
+                # stream, so reuse is ordered after this call's kernels.
+                with torch.cuda.stream(active) if stream is not None else nullcontext():
+                    scratch = torch.empty((nbytes,), dtype=torch.uint8, device=values.device)
+                base = scratch.data_ptr()
+            if stream is not None:
+                for tensor in (values, offsets, out):
+                    tensor.record_stream(active)
+            report = _native.run(self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b,
+                                 values.data_ptr(), offsets.data_ptr(), out.data_ptr(), base, nbytes, schedule,
+                                 max_len, self._flags, active.cuda_stream)
+        return self._report(schedule, selection, started, report, nbytes)
+
+    def _report(self, schedule, selection, started, report, nbytes) -> ExecutionReport:
+        if report is None:
+            names, grids, vec, tile, streams = (), (), 1, None, 1
+        else:
+            count = report.num_launches
+            names = tuple(_native.kernel_name(report.kernel_ids[i]) for i in range(count))
+            grids = tuple(tuple(int(x) for x in report.grid[i]) for i in range(count))
+            vec, tile, streams = int(report.d_vector), int(report.d_tile), int(report.streams)
+        classes = ("cta",) if schedule == "naive" else (("warp", "cta", "split") if schedule == "classified"
+                                                        else ("rows",))
+        return ExecutionReport(classes, THRESHOLDS if schedule == "classified" else (), grids, nbytes, self._digest,
+                               None, "validated", names, (time.perf_counter() - started) * 1000,
+                               cache_hit=self.cache_hit, optimizations={"requested": self.spec.optimizations.to_dict()},
+                               d_tile=tile, d_vector=vec, streams=streams, selected=schedule, selection=selection)

@@ -1,0 +1,214 @@
+"""GPU parity: every schedule of libragged_b200 against the CPU oracle.
+
+Each call goes through the public API and the C ABI (rg_run).  Results are
+checked with the reference's tolerance contract and this build's strict one
+(max bit-exact; f32 sum/softmax rtol 1e-5; bf16 within 1 ulp), outputs are
+guarded against out-of-bounds writes.  Cases restate the reference's
+test/gpu/test_correctness.py and test/gpu/test_classified.py.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from helpers import DISTRIBUTIONS, check, make_lengths, offsets_of, prepared, run_device
+from oracle import reference_port as rp
+
+pytestmark = pytest.mark.gpu
+
+
+def schedules(op):
+    from ragged.compiler import IMPLEMENTED
+    return IMPLEMENTED["softmax" if op == "softmax" else "reduce"]
+
+
+ALL = [(op, s) for op in ("sum", "max", "softmax") for s in ("naive", "classified", "rowbalanced")
+       if not (op == "softmax" and s == "rowbalanced")]
+
+
+def _run_all(cuda, op, dtype, values, offsets, **kwargs):
+    """Run every implemented schedule; check each; return the outputs."""
+    outputs = {}
+    reference = None
+    with np.errstate(all="ignore"):
+        reference = rp.REFERENCES[op](values, offsets)
+    for schedule in schedules(op):
+        actual, report = run_device(cuda, op, dtype, values, offsets, select=schedule, **kwargs)
+        assert report.selected == schedule
+        check(actual, values, offsets, op, dtype, reference)
+        outputs[schedule] = actual
+    return outputs
+
+
+def test_golden_cases(cuda, golden):
+    for name, case in golden.items():
+        for op in ("sum", "max", "softmax"):
+            for schedule in schedules(op):
+                actual, _ = run_device(cuda, op, case["dtype"], case["values"], case["offsets"], select=schedule)
+                expected = case[op]
+                with np.errstate(all="ignore"):
+                    rp.assert_matches(actual, case["values"], case["offsets"], operation=op,
+                                      input_dtype=case["dtype"], reference=expected)
+                    rp.check_strict(actual, case["values"], case["offsets"], operation=op,
+                                    input_dtype=case["dtype"], reference=expected)
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("d", [1, 2, 3, 16, 100, 128, 256, 1024])
+@pytest.mark.parametrize("index", ["i32", "i64"])
+@pytest.mark.parametrize("distribution", DISTRIBUTIONS)
+def test_matrix(cuda, op, dtype, d, index, distribution):
+    total = 4096 if d <= 256 else 1024
+    lengths = make_lengths(distribution, 64, total, seed=711)
+    offsets = offsets_of(lengths, index)
+    values = prepared(np.random.default_rng(981).normal(size=(int(offsets[-1]), d)), dtype)
+    _run_all(cuda, op, dtype, values, offsets)
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("offsets", [[0], [0, 0, 0], [0, 0, 1, 1, 4]])
+def test_empty_all_empty_and_tail_features(cuda, op, dtype, offsets):
+    values = np.arange(offsets[-1] * 3, dtype=np.float32).reshape(offsets[-1], 3)
+    _run_all(cuda, op, dtype, values, np.array(offsets, dtype=np.int64))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows", [2, 33, 64, 5000])
+def test_softmax_special_values(cuda, dtype, rows):
+    # NaN; +inf with finite; all -inf; finite with -inf; one +inf with -inf only.
+    values = np.full((rows, 5), -np.inf, dtype=np.float32)
+    values[0] = [np.nan, np.inf, -np.inf, -np.inf, np.inf]
+    values[1] = [1, 1, -np.inf, 3, -np.inf]
+    _run_all(cuda, "softmax", dtype, values, np.array([0, rows], dtype=np.int64))
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_reduction_nonfinite(cuda, op, dtype):
+    values = np.array([[np.nan, np.inf, -np.inf, -2], [1, -np.inf, -np.inf, -4]], dtype=np.float32)
+    _run_all(cuda, op, dtype, values, np.array([0, 2, 2], dtype=np.int64))
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+def test_single_very_long_segment(cuda, op):
+    values = np.tile(np.array([[1, -1, 0.5]], dtype=np.float32), (131073, 1))
+    outputs = _run_all(cuda, op, "f32", values, np.array([0, len(values)], dtype=np.int64))
+    if op == "sum":
+        for out in outputs.values():
+            np.testing.assert_array_equal(out, [[131073, -131073, 65536.5]])
+
+
+@pytest.mark.parametrize("d", [128, 1024])
+@pytest.mark.parametrize("op", ["sum", "softmax"])
+def test_long_segment_accumulation_accuracy(cuda, d, op):
+    # 0.1 is not representable: an uncompensated f32 lane accumulator drifts
+    # beyond the bound; the compensated one must not (reference
+    # test_correctness.py:201-216).
+    rows = 16384
+    if op == "sum":
+        values = np.full((rows, d), np.float32(0.1), dtype=np.float32)
+    else:
+        values = np.full((rows, d), np.float32(-np.log(10)), dtype=np.float32)
+        values[0] = 0
+    _run_all(cuda, op, "f32", values, np.array([0, rows], dtype=np.int64))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("d", [128, 1024])
+def test_compensated_sum_preserves_nonfinite(cuda, dtype, d):
+    values = np.zeros((12, d), dtype=np.float32)
+    values[0, :5] = [np.inf, -np.inf, np.inf, np.nan, 3]
+    values[4, :5] = [2, 2, -np.inf, 2, np.inf]
+    values[8, :5] = [3, 3, 3, 3, 2]
+    _run_all(cuda, "sum", dtype, values, np.array([0, 12], dtype=np.int64))
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_metamorphic_relations(cuda, op, dtype):
+    """Permutation, empty insertion, split-sum and shift invariance
+    (reference test_correctness.py:233-260), per schedule."""
+    values = np.random.default_rng(90).integers(-4, 5, size=(39, 7)).astype(np.float32)
+    offsets = np.array([0, 3, 3, 30, 39], dtype=np.int64)
+    for schedule in schedules(op):
+        run = lambda v, o: run_device(cuda, op, dtype, v, np.asarray(o, dtype=np.int64), select=schedule)[0]
+        original = run(values, offsets)
+        pieces = [values[a:b] for a, b in zip(offsets[:-1], offsets[1:])]
+        permutation = [3, 1, 0, 2]
+        permuted_values = np.concatenate([pieces[i] for i in permutation])
+        permuted_offsets = [0, *np.cumsum([len(pieces[i]) for i in permutation])]
+        permuted = run(permuted_values, permuted_offsets)
+        expected = (np.concatenate([original[offsets[i]:offsets[i + 1]] for i in permutation])
+                    if op == "softmax" else original[permutation])
+        np.testing.assert_array_equal(permuted, expected)
+        inserted = run(values, [0, 0, 3, 3, 30, 39, 39])
+        np.testing.assert_array_equal(inserted if op == "softmax" else inserted[1:5], original)
+        if op == "softmax":
+            shifted = run(values + 5, offsets)
+            np.testing.assert_allclose(shifted, original, rtol=2e-5 if dtype == "f32" else 2e-2,
+                                       atol=2e-6 if dtype == "f32" else 2e-3)
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+def test_threshold_boundaries(cuda, op):
+    """Segment lengths at and around every class bound (reference
+    test_classified.py:23): 0, 1, 31-33, 4095-4097 and a split one."""
+    lengths = np.array([0, 1, 31, 32, 33, 4095, 4096, 4097, 20000, 2, 0], dtype=np.int64)
+    offsets = offsets_of(lengths)
+    values = np.random.default_rng(17).normal(size=(int(offsets[-1]), 64)).astype(np.float32)
+    _run_all(cuda, op, "f32", values, offsets)
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+def test_unvectorized_program(cuda, op):
+    lengths = make_lengths("long_tail", 40, 3000, seed=3)
+    offsets = offsets_of(lengths)
+    values = np.random.default_rng(4).normal(size=(int(offsets[-1]), 16)).astype(np.float32)
+    actual, report = run_device(cuda, op, "f32", values, offsets, vectorize=False, select="naive")
+    assert report.d_vector == 1
+    check(actual, values, offsets, op, "f32")
+
+
+def test_nondefault_stream(cuda):
+    torch = cuda
+    lengths = make_lengths("uniform", 100, 20000, seed=9)
+    offsets = offsets_of(lengths)
+    values = np.random.default_rng(10).normal(size=(int(offsets[-1]), 128)).astype(np.float32)
+    stream = torch.cuda.Stream()
+    for op in ("sum", "max", "softmax"):
+        actual, _ = run_device(cuda, op, "f32", values, offsets, stream=stream)
+        check(actual, values, offsets, op, "f32")
+
+
+def test_misaligned_view_is_rejected(cuda):
+    torch = cuda
+    from helpers import program
+    from ragged import ValidationError
+    prog = program("sum", "f32", 128, "i64")
+    base = torch.zeros((11, 128), device="cuda")
+    values = base.view(-1)[1:1 + 10 * 128].view(10, 128)  # 4-byte offset
+    offsets = torch.tensor([0, 10], device="cuda")
+    out = torch.empty((1, 128), device="cuda")
+    with pytest.raises(ValidationError, match="aligned"):
+        prog.run(values, offsets, out)
+
+
+def test_validation_errors(cuda):
+    torch = cuda
+    from helpers import program
+    from ragged import RuntimeUnavailable, ValidationError
+    prog = program("sum", "f32", 4, "i64")
+    values = torch.zeros((5, 4), device="cuda")
+    offsets = torch.tensor([0, 5], device="cuda")
+    with pytest.raises(ValidationError, match="out shape"):
+        prog.run(values, offsets, torch.empty((2, 4), device="cuda"))
+    with pytest.raises(ValidationError, match="dtype"):
+        prog.run(values, offsets.int(), torch.empty((1, 4), device="cuda"))
+    with pytest.raises(RuntimeUnavailable, match="CUDA device"):
+        prog.run(values.cpu(), offsets, torch.empty((1, 4), device="cuda"))
+    with pytest.raises(ValidationError, match="alias"):
+        prog.run(values, offsets, values[:1])
+    with pytest.raises(RuntimeUnavailable, match="checked"):
+        prog.run(values, offsets, torch.empty((1, 4), device="cuda"), mode="checked")

@@ -1,0 +1,133 @@
+"""Host-side contracts of the drop-in API (no GPU needed).
+
+Restates the reference's frontend / cache / selection host tests
+(test/python/test_frontend.py, test_cache_adversarial.py,
+test_selection.py) for this build.
+"""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from ragged import (ArtifactCache, CacheMismatch, CompilationError, Compiler, Hints, Optimizations, ProgramSpec,
+                    SpecializationLimit, ValidationError)
+from ragged import selection, workloads
+from ragged.compiler import schedules_for
+
+
+@pytest.mark.parametrize("kwargs,match", [
+    (dict(op="mean"), "op must"), (dict(op="sum", dtype="f16"), "dtype"), (dict(op="sum", feature_dim=0), "feature_dim"),
+    (dict(op="sum", feature_dim=1025), "feature_dim"), (dict(op="sum", offsets_dtype="u32"), "offsets_dtype"),
+    (dict(op="sum", strategy="fast"), "strategy"), (dict(op="sum", alias="inplace"), "in-place"),
+    (dict(op="sum", chip="sm_89"), "chip"), (dict(op="max", mask=True), "mask"),
+    (dict(op="sum", scale=float("inf")), "scale")])
+def test_spec_validation(kwargs, match):
+    with pytest.raises(ValidationError, match=match):
+        ProgramSpec(**kwargs)
+
+
+def test_hints_and_optimizations_validation():
+    with pytest.raises(ValidationError):
+        Hints(max_len=-1)
+    with pytest.raises(ValidationError):
+        Hints(min_len=5, max_len=4)
+    with pytest.raises(ValidationError):
+        Optimizations(vectorize=1)
+    with pytest.raises(ValidationError):
+        Optimizations(feature_tile=3)
+
+
+@pytest.mark.parametrize("d,dtype,expected", [(128, "f32", (32, 4)), (128, "bf16", (16, 8)), (1, "f32", (1, 1)),
+                                              (2, "f32", (1, 2)), (3, "bf16", (4, 1)), (1024, "f32", (32, 4)),
+                                              (100, "f32", (32, 4)), (256, "bf16", (32, 8))])
+def test_geometry(d, dtype, expected):
+    assert Optimizations().geometry(d, dtype) == expected
+
+
+def test_spec_roundtrip_and_hash():
+    spec = ProgramSpec("softmax", "bf16", 128, "i64", hints=Hints(max_len=7))
+    assert ProgramSpec.from_dict(spec.to_dict()) == spec
+    assert spec.ir_hash != ProgramSpec("softmax", "bf16", 128, "i32").ir_hash
+    assert spec.signature == "softmax:bf16:D128:i64:sm_100a"
+
+
+def test_compile_cache_hit_and_adaptive(tmp_path, native_library):
+    cache = ArtifactCache(tmp_path)
+    spec = ProgramSpec("sum", "f32", 128)
+    first = Compiler().compile(spec, cache)
+    second = Compiler().compile(spec, cache)
+    assert not first.cache_hit and second.cache_hit
+    assert second.schedules == first.schedules
+    naive = Compiler().compile(ProgramSpec("sum", "f32", 128, strategy="naive"), cache)
+    assert naive.schedules == ("naive",) and not naive.selects
+
+
+def test_unsupported_features_fail_to_compile(tmp_path, native_library):
+    cache = ArtifactCache(tmp_path)
+    for spec in (ProgramSpec("softmax", mask=True), ProgramSpec("softmax", alias="inplace"),
+                 ProgramSpec("sum", scale=2.0), ProgramSpec("sum", debug_visits=True)):
+        with pytest.raises(CompilationError, match="not implemented"):
+            Compiler().compile(spec, cache)
+
+
+def test_cache_rejects_tampering_and_limits(tmp_path, native_library):
+    cache = ArtifactCache(tmp_path, max_specializations=2)
+    Compiler().compile(ProgramSpec("sum", "f32", 8, strategy="naive"), cache)
+    Compiler().compile(ProgramSpec("sum", "f32", 8, hints=Hints(max_len=3), strategy="naive"), cache)
+    with pytest.raises(SpecializationLimit):
+        Compiler().compile(ProgramSpec("sum", "f32", 8, hints=Hints(max_len=4), strategy="naive"), cache)
+    entry = next(p for p in tmp_path.rglob("manifest.json"))
+    manifest = json.loads(entry.read_text())
+    manifest["metadata"]["schedules"] = ["rowbalanced"]
+    entry.write_text(json.dumps(manifest))
+    with pytest.raises(CacheMismatch, match="SHA256"):
+        for max_len in (None, 3):
+            Compiler().compile(ProgramSpec("sum", "f32", 8, hints=Hints(max_len=max_len), strategy="naive"), cache)
+
+
+def test_schedules_for():
+    assert schedules_for(ProgramSpec("sum", strategy="naive")) == ["naive"]
+    assert schedules_for(ProgramSpec("sum", optimizations=Optimizations(classification=False))) == ["naive"]
+
+
+def test_cost_model_terms_and_choice():
+    terms = selection.features(n=2**18, b=1000, d=1, max_len=4000, span=1, element_bytes=4, op="sum", l2_mib=1.0)
+    assert terms[0] == 1.0 and terms[1] == 1.0 and terms[3] == 1.0
+    assert terms[4] == pytest.approx(np.log2(4000 * 1000 / 2**18))
+    assert terms[5] == pytest.approx(1.0 + 1000 * 4 / 2**20 - 1.0)
+    model = selection.CostModel.from_dict({
+        "version": 3, "margin": 0.1, "l2_mib": 100.0,
+        "coefficients": {"reduce": {"rowbalanced": [10, 0, 0, 0, 0, 0], "naive": [5, 0, 0, 0, 0, 0]},
+                         "softmax": {"classified": [10, 0, 0, 0, 0, 0], "naive": [9.5, 0, 0, 0, 0, 0]}}})
+    assert model.choose("sum", 100, 10, 4, None, 4)[0] == "rowbalanced"     # no length statistics
+    assert model.choose("sum", 100, 10, 4, 50, 4)[0] == "naive"            # 5 < 10 * 0.9
+    assert model.choose("softmax", 100, 10, 4, 50, 4)[0] == "classified"   # 9.5 is within the margin
+    with pytest.raises(CacheMismatch):
+        selection.CostModel.from_dict({"version": 3, "margin": 0.0, "l2_mib": 1.0,
+                                       "coefficients": {"reduce": {"rowbalanced": [-1] * 6},
+                                                        "softmax": {"classified": [0] * 6}}})
+
+
+def test_shipped_cost_model_loads():
+    model = selection.default_model()
+    assert set(model.coefficients) == {"reduce", "softmax"}
+
+
+@pytest.mark.parametrize("name", workloads.CONFIGS)
+def test_workload_generators(name):
+    w = workloads.make(name, scale=0.01)
+    offsets = w.offsets()
+    assert offsets[0] == 0 and offsets[-1] == w.n and np.all(np.diff(offsets.astype(np.int64)) >= 0)
+    values = w.host_values(slice(0, 100))
+    assert values.shape == (min(100, w.n), w.d)
+
+
+def test_full_size_workloads_match_configuration():
+    assert workloads.make("c1").n == 1_058_479
+    c2 = workloads.make("c2_max")
+    assert c2.n == 12_800_000 and c2.b == 200_000 and int((c2.lengths == 0).sum()) == 2000
+    c5 = workloads.make("c5")
+    assert c5.n == 200_000_000 and c5.b == 4_000_000 and c5.lengths.max() == 50_000_000
+    assert int((c5.lengths > c5.n // 8).sum()) == 3
