@@ -105,10 +105,10 @@ const char *rg_last_error(void);
 int rg_get_device_info(int device, rg_device_info *info);
 
 /* Scratch bytes rg_run needs for this problem on the current device (0 for
- * the block-per-segment schedule).  Replaces the workspace sizing of the
+ * the block-per-segment schedule); `flags` as for rg_run.  Replaces the workspace sizing of the
  * reference's layout.py:186-243 (resolve_layout) and runtime.py:534-542. */
 int rg_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
-                       int schedule, int64_t max_len, int64_t *bytes);
+                       int schedule, int64_t max_len, uint32_t flags, int64_t *bytes);
 
 /* Launch one segmented operation on `stream` (a cudaStream_t; NULL = the
  * legacy default stream).  `workspace` must hold rg_workspace_bytes() bytes

@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace rgb {
 
 enum Op : int { OP_SUM = 0, OP_MAX = 1, OP_SOFTMAX = 2 };
@@ -166,23 +168,26 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// Global loads of VEC elements into f32, read-only path.
+// Global loads of VEC elements, read-only path.  `Raw` is the loaded
+// register form (kept while loads are in flight), `unpack` converts it to
+// f32; `load` does both.
 template <typename T, int VEC>
 struct VecIO;
 
 template <int VEC>
 struct VecIO<float, VEC> {
-  static __device__ __forceinline__ void load(const float *p, float (&x)[VEC]) {
+  using Raw = typename std::conditional<VEC == 4, float4, typename std::conditional<VEC == 2, float2, float>::type>::type;
+  static __device__ __forceinline__ Raw load_raw(const float *p) { return __ldg(reinterpret_cast<const Raw *>(p)); }
+  static __device__ __forceinline__ void unpack(const Raw &v, float (&x)[VEC]) {
     if constexpr (VEC == 4) {
-      const float4 v = __ldg(reinterpret_cast<const float4 *>(p));
       x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
     } else if constexpr (VEC == 2) {
-      const float2 v = __ldg(reinterpret_cast<const float2 *>(p));
       x[0] = v.x; x[1] = v.y;
     } else {
-      x[0] = __ldg(p);
+      x[0] = v;
     }
   }
+  static __device__ __forceinline__ void load(const float *p, float (&x)[VEC]) { unpack(load_raw(p), x); }
   static __device__ __forceinline__ void store(float *p, const float (&x)[VEC]) {
     if constexpr (VEC == 4) {
       *reinterpret_cast<float4 *>(p) = make_float4(x[0], x[1], x[2], x[3]);
@@ -196,22 +201,26 @@ struct VecIO<float, VEC> {
 
 template <int VEC>
 struct VecIO<__nv_bfloat16, VEC> {
-  static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&x)[VEC]) {
+  using Raw = typename std::conditional<
+      VEC == 8, uint4,
+      typename std::conditional<VEC == 4, uint2,
+                                typename std::conditional<VEC == 2, unsigned int, unsigned short>::type>::type>::type;
+  static __device__ __forceinline__ Raw load_raw(const __nv_bfloat16 *p) {
+    return __ldg(reinterpret_cast<const Raw *>(p));
+  }
+  static __device__ __forceinline__ void unpack(const Raw &v, float (&x)[VEC]) {
     if constexpr (VEC == 8) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
       x[0] = bf16_lo(v.x); x[1] = bf16_hi(v.x); x[2] = bf16_lo(v.y); x[3] = bf16_hi(v.y);
       x[4] = bf16_lo(v.z); x[5] = bf16_hi(v.z); x[6] = bf16_lo(v.w); x[7] = bf16_hi(v.w);
     } else if constexpr (VEC == 4) {
-      const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
       x[0] = bf16_lo(v.x); x[1] = bf16_hi(v.x); x[2] = bf16_lo(v.y); x[3] = bf16_hi(v.y);
     } else if constexpr (VEC == 2) {
-      const uint32_t v = __ldg(reinterpret_cast<const unsigned int *>(p));
       x[0] = bf16_lo(v); x[1] = bf16_hi(v);
     } else {
-      const unsigned short v = __ldg(reinterpret_cast<const unsigned short *>(p));
       x[0] = __uint_as_float(static_cast<uint32_t>(v) << 16);
     }
   }
+  static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&x)[VEC]) { unpack(load_raw(p), x); }
   static __device__ __forceinline__ void store(__nv_bfloat16 *p, const float (&x)[VEC]) {
     if constexpr (VEC == 8) {
       *reinterpret_cast<uint4 *>(p) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),

@@ -66,5 +66,7 @@ int device_props(DeviceProps *props);  // current device
 
 // Per-schedule entry points (launch on stream, record into report).
 int launch_naive(const Problem &p, const Geometry &g, cudaStream_t stream, rg_report *report);
+int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
+int launch_rowbal(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
 
 }  // namespace rgb

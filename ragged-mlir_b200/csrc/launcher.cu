@@ -146,12 +146,14 @@ static int check_device(DeviceProps *props) {
   return RG_OK;
 }
 
-static int64_t workspace_for(const Problem &p, int schedule, const DeviceProps &dev) {
-  (void)dev;
+// Scratch bytes of `schedule` for this problem (status on failure).
+static int workspace_for(const Problem &p, const Geometry &g, int schedule, int64_t *bytes) {
+  *bytes = 0;
   switch (schedule) {
-    case RG_SCHEDULE_NAIVE: return 0;
-    default: return -1;
+    case RG_SCHEDULE_NAIVE: return RG_OK;
+    case RG_SCHEDULE_ROWBALANCED: return rowbal_workspace(p, g, bytes);
   }
+  return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
 }
 
 }  // namespace rgb
@@ -213,9 +215,9 @@ int rg_get_device_info(int device, rg_device_info *info) {
 }
 
 int rg_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int schedule,
-                       int64_t max_len, int64_t *bytes) {
+                       int64_t max_len, uint32_t flags, int64_t *bytes) {
   if (!bytes) return fail(RG_ERR_INVALID_ARGUMENT, "bytes is NULL");
-  Problem p{op, dtype, index_dtype, d, n, b, nullptr, nullptr, nullptr, max_len, 0};
+  Problem p{op, dtype, index_dtype, d, n, b, nullptr, nullptr, nullptr, max_len, flags};
   // Pointer-free validation: shapes only.
   if (op < RG_OP_SUM || op > RG_OP_SOFTMAX || (dtype != RG_DTYPE_F32 && dtype != RG_DTYPE_BF16) ||
       (index_dtype != RG_INDEX_I32 && index_dtype != RG_INDEX_I64) || d < 1 || d > 1024 || n < 0 || b < 0)
@@ -223,10 +225,7 @@ int rg_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n,
   DeviceProps dev;
   int status = check_device(&dev);
   if (status) return status;
-  const int64_t ws = workspace_for(p, schedule, dev);
-  if (ws < 0) return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
-  *bytes = ws;
-  return RG_OK;
+  return workspace_for(p, make_geometry(p), schedule, bytes);
 }
 
 int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, const void *values,
@@ -249,8 +248,9 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, 
   DeviceProps dev;
   status = check_device(&dev);
   if (status) return status;
-  const int64_t need = workspace_for(p, schedule, dev);
-  if (need < 0) return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
+  int64_t need = 0;
+  status = workspace_for(p, g, schedule, &need);
+  if (status) return status;
   if (report) report->workspace_bytes = need;
   if (need > 0) {
     if (!workspace || workspace_bytes < need) return fail(RG_ERR_WORKSPACE, "workspace missing or too small");
@@ -259,6 +259,7 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (schedule) {
     case RG_SCHEDULE_NAIVE: return launch_naive(p, g, s, report);
+    case RG_SCHEDULE_ROWBALANCED: return launch_rowbal(p, g, workspace, s, report);
   }
   return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
 }

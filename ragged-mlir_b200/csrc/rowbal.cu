@@ -1,0 +1,145 @@
+// Planning, workspace layout and launch of the row-balanced schedule.
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "internal.h"
+#include "rowbal.cuh"
+
+namespace rgb {
+
+namespace {
+
+std::mutex g_occupancy_mutex;
+std::map<std::pair<const void *, int>, int> g_occupancy;  // (kernel, device) -> blocks per SM
+
+int occupancy(const void *kernel, int device, int threads, int *blocks) {
+  const auto key = std::make_pair(kernel, device);
+  std::lock_guard<std::mutex> lock(g_occupancy_mutex);
+  auto it = g_occupancy.find(key);
+  if (it != g_occupancy.end()) {
+    *blocks = it->second;
+    return RG_OK;
+  }
+  int n = 0;
+  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0),
+                          "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (status) return status;
+  g_occupancy[key] = n < 1 ? 1 : n;
+  *blocks = g_occupancy[key];
+  return RG_OK;
+}
+
+template <typename T, typename OffT, int OP, int VEC>
+const void *kernel_ptr() {
+  return reinterpret_cast<const void *>(&rowbal_kernel<T, OffT, OP, VEC>);
+}
+
+constexpr int64_t kAlign = 256;
+int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct Plan {
+  int64_t units;
+  int ctas;
+  int64_t pieces_bytes, meta_bytes;
+};
+
+// Units: enough CTAs for one resident wave (per column tile), but no more
+// than one unit per 64 path items.
+int make_plan(const Problem &p, const Geometry &g, const void *kernel, Plan *plan) {
+  DeviceProps dev;
+  int status = device_props(&dev);
+  if (status) return status;
+  int per_sm = 0;
+  status = occupancy(kernel, dev.device, kRowbalThreads, &per_sm);
+  if (status) return status;
+  const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
+  int64_t ctas = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
+  if (ctas < 1) ctas = 1;
+  const int64_t path = p.n + p.b;
+  const int64_t wanted = (path + 64 * units_per_cta - 1) / (64 * units_per_cta);
+  if (wanted < ctas) ctas = wanted < 1 ? 1 : wanted;
+  plan->ctas = static_cast<int>(ctas);
+  plan->units = ctas * units_per_cta;
+  const int width = p.op == RG_OP_SUM ? 2 : 1;
+  plan->pieces_bytes = align_up(plan->units * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
+  plan->meta_bytes = align_up(plan->units * static_cast<int64_t>(sizeof(UnitMeta)));
+  return RG_OK;
+}
+
+template <typename T, typename OffT, int OP, int VEC>
+int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *bytes, cudaStream_t stream,
+              rg_report *report) {
+  Plan plan;
+  int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC>(), &plan);
+  if (status) return status;
+  if (bytes) {
+    *bytes = plan.pieces_bytes + plan.meta_bytes;
+    return RG_OK;
+  }
+  float *pieces = static_cast<float *>(workspace);
+  UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
+  dim3 grid(plan.ctas, g.col_tiles, 1);
+  rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, 0, stream>>>(
+      static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
+      p.d, g.g_shift, g.vec_cols, plan.units, pieces, meta);
+  record_launch(report, K_ROWBAL, grid, kRowbalThreads, 0);
+  status = check_cuda(cudaGetLastError(), "rowbal_kernel launch");
+  if (status || plan.units < 2) return status;
+  dim3 fix_grid(static_cast<unsigned>(plan.units), g.col_tiles, 1);
+  rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, 32, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols, plan.units,
+                                                               pieces, meta);
+  record_launch(report, K_ROWBAL_FIXUP, fix_grid, 32, 0);
+  return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
+}
+
+template <typename T, typename OffT, int OP>
+int run_vec(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cudaStream_t s, rg_report *r) {
+  switch (g.vec) {
+    case 1: return run_typed<T, OffT, OP, 1>(p, g, ws, bytes, s, r);
+    case 2: return run_typed<T, OffT, OP, 2>(p, g, ws, bytes, s, r);
+    case 4: return run_typed<T, OffT, OP, 4>(p, g, ws, bytes, s, r);
+    case 8:
+      if constexpr (sizeof(T) == 2) return run_typed<T, OffT, OP, 8>(p, g, ws, bytes, s, r);
+      break;
+  }
+  return fail(RG_ERR_INVALID_ARGUMENT, "unsupported vector width");
+}
+
+template <typename T, typename OffT>
+int run_op(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cudaStream_t s, rg_report *r) {
+  switch (p.op) {
+    case RG_OP_SUM: return run_vec<T, OffT, OP_SUM>(p, g, ws, bytes, s, r);
+    case RG_OP_MAX: return run_vec<T, OffT, OP_MAX>(p, g, ws, bytes, s, r);
+  }
+  return fail(RG_ERR_UNSUPPORTED, "the row-balanced schedule computes sum and max only");
+}
+
+template <typename T>
+int run_index(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cudaStream_t s, rg_report *r) {
+  return p.index_dtype == RG_INDEX_I32 ? run_op<T, int32_t>(p, g, ws, bytes, s, r)
+                                       : run_op<T, int64_t>(p, g, ws, bytes, s, r);
+}
+
+int dispatch(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cudaStream_t s, rg_report *r) {
+  return p.dtype == RG_DTYPE_F32 ? run_index<float>(p, g, ws, bytes, s, r)
+                                 : run_index<__nv_bfloat16>(p, g, ws, bytes, s, r);
+}
+
+}  // namespace
+
+int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes) {
+  if (p.op == RG_OP_SOFTMAX) return fail(RG_ERR_UNSUPPORTED, "the row-balanced schedule computes sum and max only");
+  if (p.b == 0) {
+    *bytes = 0;
+    return RG_OK;
+  }
+  return dispatch(p, g, nullptr, bytes, nullptr, nullptr);
+}
+
+int launch_rowbal(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report) {
+  if (p.b == 0) return RG_OK;
+  return dispatch(p, g, workspace, nullptr, stream, report);
+}
+
+}  // namespace rgb

@@ -73,7 +73,7 @@ def library(path: Path | None = None):
         lib.rg_kernel_name.argtypes = [i32]
         lib.rg_get_device_info.argtypes = [i32, ctypes.POINTER(DeviceInfo)]
         lib.rg_get_device_info.restype = i32
-        lib.rg_workspace_bytes.argtypes = [i32, i32, i32, i64, i64, i64, i32, i64, ctypes.POINTER(i64)]
+        lib.rg_workspace_bytes.argtypes = [i32, i32, i32, i64, i64, i64, i32, i64, u32, ctypes.POINTER(i64)]
         lib.rg_workspace_bytes.restype = i32
         lib.rg_run.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, p, i64, i32, i64, u32, p,
                                ctypes.POINTER(Report)]
@@ -116,10 +116,10 @@ def device_info(device: int) -> DeviceInfo:
 
 
 def workspace_bytes(op: str, dtype: str, index: str, d: int, n: int, b: int, schedule: str,
-                    max_len: int | None) -> int:
+                    max_len: int | None, flags: int = 0) -> int:
     out = ctypes.c_int64(0)
     raise_for(library().rg_workspace_bytes(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, SCHEDULES[schedule],
-                                           -1 if max_len is None else max_len, ctypes.byref(out)),
+                                           -1 if max_len is None else max_len, flags, ctypes.byref(out)),
               "rg_workspace_bytes")
     return int(out.value)
 

@@ -162,7 +162,8 @@ class CompiledProgram:
             if len(self._workspace) >= 256:
                 self._workspace.clear()
             nbytes = self._workspace[key] = _native.workspace_bytes(
-                self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b, schedule, max_len)
+                self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b, schedule, max_len,
+                self._flags)
         return nbytes
 
     def run(self, values, offsets, out, stream=None, mode: str = "validated", *,
