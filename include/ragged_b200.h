@@ -124,6 +124,20 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
 /* Name of a kernel id reported in rg_report.kernel_ids ("" if unknown). */
 const char *rg_kernel_name(int kernel_id);
 
+/* Row-balanced segmented sum or max that allocates nothing and takes no
+ * workspace: for callers that may not allocate device memory (a host that
+ * reserves all device memory for its own pool, a plugin callback that may
+ * not allocate, a path that cannot afford cudaMalloc's synchronisation).
+ * It has no counterpart in the reference.  Its scratch is a static 8 MiB
+ * device array per GPU, held until the process exits; the unit count is
+ * reduced to fit it (RG_ERR_WORKSPACE if even one CTA per SM would not).
+ * The first call on a device resolves the array's address and should come
+ * before any stream capture.  All calls on a device share the array, so
+ * calls that overlap on the GPU race; nothing in it needs zeroing.
+ * Arguments as for rg_run (sum and max only). */
+int rg_run_noalloc(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
+                   const void *values, const void *offsets, void *out, uint32_t flags, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -63,6 +63,8 @@ int check_cuda(cudaError_t err, const char *what);
 int elem_bytes(int dtype);
 Geometry make_geometry(const Problem &p);
 int device_props(DeviceProps *props);  // current device
+int validate(const Problem &p);           // argument checks of rg_run
+int check_device(DeviceProps *props);     // current device must be sm_100
 
 // Per-schedule entry points (launch on stream, record into report).
 int launch_naive(const Problem &p, const Geometry &g, cudaStream_t stream, rg_report *report);

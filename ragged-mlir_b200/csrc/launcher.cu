@@ -91,7 +91,7 @@ int device_props(DeviceProps *props) {
   return RG_OK;
 }
 
-static int validate(const Problem &p) {
+int validate(const Problem &p) {
   if (p.op < RG_OP_SUM || p.op > RG_OP_SOFTMAX) return fail(RG_ERR_INVALID_ARGUMENT, "op must be sum, max or softmax");
   if (p.dtype != RG_DTYPE_F32 && p.dtype != RG_DTYPE_BF16)
     return fail(RG_ERR_INVALID_ARGUMENT, "dtype must be f32 or bf16");
@@ -133,7 +133,7 @@ static int validate(const Problem &p) {
   return RG_OK;
 }
 
-static int check_device(DeviceProps *props) {
+int check_device(DeviceProps *props) {
   int status = device_props(props);
   if (status) return status;
   if (props->cc_major != 10 || props->cc_minor != 0) {

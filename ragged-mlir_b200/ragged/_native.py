@@ -29,7 +29,7 @@ MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.
 EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
-            "rg_run", "rg_kernel_name")
+            "rg_run", "rg_kernel_name", "rg_run_noalloc")
 
 
 class Report(ctypes.Structure):
@@ -78,6 +78,8 @@ def library(path: Path | None = None):
         lib.rg_run.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, p, i64, i32, i64, u32, p,
                                ctypes.POINTER(Report)]
         lib.rg_run.restype = i32
+        lib.rg_run_noalloc.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, u32, p]
+        lib.rg_run_noalloc.restype = i32
         _lib = lib
         return lib
 
