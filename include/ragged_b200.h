@@ -129,7 +129,7 @@ const char *rg_kernel_name(int kernel_id);
  * reserves all device memory for its own pool, a plugin callback that may
  * not allocate, a path that cannot afford cudaMalloc's synchronisation).
  * It has no counterpart in the reference.  Its scratch is a static 8 MiB
- * device array per GPU, held until the process exits; the unit count is
+ * device array per GPU, held until the process exits; the CTA count is
  * reduced to fit it (RG_ERR_WORKSPACE if even one CTA per SM would not).
  * The first call on a device resolves the array's address and should come
  * before any stream capture.  All calls on a device share the array, so

@@ -235,6 +235,34 @@ struct VecIO<__nv_bfloat16, VEC> {
   }
 };
 
+// --------------------------------------------------------------- cp.async --
+//
+// Asynchronous global -> shared copies of 4, 8 or 16 bytes (L1 bypassed for
+// 16); completion is per thread (commit / wait_group).
+
+template <int BYTES>
+__device__ __forceinline__ void cp_async(uint32_t smem_addr, const void *gmem) {
+  static_assert(BYTES == 4 || BYTES == 8 || BYTES == 16 || BYTES == 2, "cp.async size");
+  if constexpr (BYTES == 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr), "l"(gmem) : "memory");
+  } else if constexpr (BYTES == 8) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_addr), "l"(gmem) : "memory");
+  } else if constexpr (BYTES == 4) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_addr), "l"(gmem) : "memory");
+  } else {
+    // 2-byte elements (bf16, one per thread): a plain load and shared store.
+    *reinterpret_cast<unsigned short *>(__cvta_shared_to_generic(smem_addr)) =
+        __ldg(reinterpret_cast<const unsigned short *>(gmem));
+  }
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 // ------------------------------------------------------------ accumulators --
 //
 // One accumulator per thread covers VEC adjacent features of one column.

@@ -11,11 +11,11 @@
 // the row-balanced schedule) lives in `g_static_scratch`, a fixed 8 MiB
 // array that every GPU loading the library holds until the process exits.
 //
-// * Size limit: the unit count is reduced until the pieces fit in 8 MiB,
-//   down to one CTA per SM; a problem whose pieces for that many units
-//   would still not fit is rejected with RG_ERR_WORKSPACE and the byte
-//   counts.  On a 148-SM B200 every D <= 1024 fits (the largest need,
-//   f32 sum with D = 1024, is about 2.5 MiB).
+// * Size limit: the CTA count is reduced until the pieces (two per CTA)
+//   fit in 8 MiB, down to one CTA per SM; a problem whose pieces would
+//   still not fit is rejected with RG_ERR_WORKSPACE and the byte counts.
+//   On a 148-SM B200 every D <= 1024 fits with room to spare (an f32 sum
+//   with D = 1024 needs 16 KiB per CTA).
 // * Set-up: the first call on each device resolves the array's device
 //   address with cudaGetSymbolAddress (with that device current) and caches
 //   it; make that first call before any stream capture.
@@ -60,15 +60,15 @@ int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 template <typename T, typename OffT, int OP, int VEC>
 int run_typed(const Problem &p, const Geometry &g, const DeviceProps &dev, void *scratch, cudaStream_t stream) {
   int per_sm = 0;
-  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                              &per_sm, rowbal_kernel<T, OffT, OP, VEC>, kRowbalThreads, 0),
-                          "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowbal_kernel<T, OffT, OP, VEC>,
+                                                                    kRowbalThreads, kRowbalSmem),
+                      "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   if (status) return status;
   if (per_sm < 1) per_sm = 1;
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
   const int width = OP == OP_SUM ? 2 : 1;
   const int64_t unit_piece_bytes = 2 * width * p.d * static_cast<int64_t>(sizeof(float));
-  const int64_t cta_bytes = units_per_cta * (unit_piece_bytes + static_cast<int64_t>(sizeof(UnitMeta)));
+  const int64_t cta_bytes = unit_piece_bytes + static_cast<int64_t>(sizeof(UnitMeta));  // per CTA
   // As the standard plan: one resident wave, no more than one unit per 64 path items ...
   int64_t ctas = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
   if (ctas < 1) ctas = 1;
@@ -91,16 +91,16 @@ int run_typed(const Problem &p, const Geometry &g, const DeviceProps &dev, void 
   if (ctas > fit) ctas = fit;
   const int64_t units = ctas * units_per_cta;
   float *pieces = static_cast<float *>(scratch);
-  UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(scratch) + align256(units * unit_piece_bytes));
+  UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(scratch) + align256(ctas * unit_piece_bytes));
   dim3 grid(static_cast<unsigned>(ctas), g.col_tiles, 1);
-  rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, 0, stream>>>(
+  rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
       p.d, g.g_shift, g.vec_cols, units, pieces, meta);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch (no-alloc)");
-  if (status || units < 2) return status;
-  dim3 fix_grid(static_cast<unsigned>(units), g.col_tiles, 1);
-  rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, 32, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols, units,
-                                                               pieces, meta);
+  if (status || ctas < 2) return status;
+  dim3 fix_grid(static_cast<unsigned>(ctas), g.col_tiles, 1);
+  rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d,
+                                                                          g.vec_cols, ctas, pieces, meta);
   return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch (no-alloc)");
 }
 

@@ -13,6 +13,8 @@ namespace {
 std::mutex g_occupancy_mutex;
 std::map<std::pair<const void *, int>, int> g_occupancy;  // (kernel, device) -> blocks per SM
 
+// Opt the kernel into its dynamic shared memory (once per device) and
+// return its resident CTAs per SM.
 int occupancy(const void *kernel, int device, int threads, int *blocks) {
   const auto key = std::make_pair(kernel, device);
   std::lock_guard<std::mutex> lock(g_occupancy_mutex);
@@ -22,8 +24,8 @@ int occupancy(const void *kernel, int device, int threads, int *blocks) {
     return RG_OK;
   }
   int n = 0;
-  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0),
-                          "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, kRowbalSmem),
+                      "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   if (status) return status;
   g_occupancy[key] = n < 1 ? 1 : n;
   *blocks = g_occupancy[key];
@@ -62,8 +64,8 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, Plan *pla
   plan->ctas = static_cast<int>(ctas);
   plan->units = ctas * units_per_cta;
   const int width = p.op == RG_OP_SUM ? 2 : 1;
-  plan->pieces_bytes = align_up(plan->units * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
-  plan->meta_bytes = align_up(plan->units * static_cast<int64_t>(sizeof(UnitMeta)));
+  plan->pieces_bytes = align_up(ctas * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
+  plan->meta_bytes = align_up(ctas * static_cast<int64_t>(sizeof(UnitMeta)));
   return RG_OK;
 }
 
@@ -80,16 +82,16 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   float *pieces = static_cast<float *>(workspace);
   UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
   dim3 grid(plan.ctas, g.col_tiles, 1);
-  rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, 0, stream>>>(
+  rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
       p.d, g.g_shift, g.vec_cols, plan.units, pieces, meta);
-  record_launch(report, K_ROWBAL, grid, kRowbalThreads, 0);
+  record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch");
-  if (status || plan.units < 2) return status;
-  dim3 fix_grid(static_cast<unsigned>(plan.units), g.col_tiles, 1);
-  rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, 32, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols, plan.units,
-                                                               pieces, meta);
-  record_launch(report, K_ROWBAL_FIXUP, fix_grid, 32, 0);
+  if (status || plan.ctas < 2) return status;
+  dim3 fix_grid(static_cast<unsigned>(plan.ctas), g.col_tiles, 1);
+  rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols,
+                                                                          plan.ctas, pieces, meta);
+  record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
   return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
 }
 

@@ -16,11 +16,14 @@
 // its own contiguous rows (one 16-byte vector per lane per row), so every
 // segment that starts and ends inside a unit is reduced entirely in that
 // unit's registers and stored directly -- no shuffles or shared memory on
-// the common path.  A segment cut by a unit boundary leaves f32 pieces: the
-// unit where it starts writes a TAIL piece, units it covers completely write
-// THROUGH pieces and the unit that consumes its end writes a HEAD piece.
-// The fix-up kernel merges each cut segment's pieces in row order and
-// writes its output once (one rounding to the output dtype), so results are
+// the common path.  A segment cut by a unit boundary leaves f32 pieces in
+// shared memory: the unit where it starts a TAIL piece, units it covers
+// completely THROUGH pieces and the unit that consumes its end a HEAD
+// piece.  At the end the CTA merges its units' pieces in row order,
+// finishing every segment cut only inside the CTA, and leaves at most one
+// HEAD and one TAIL/THROUGH piece per CTA in global memory.  The fix-up
+// kernel merges each segment cut by CTA boundaries in row order and writes
+// its output once (one rounding to the output dtype), so results are
 // deterministic.
 #pragma once
 
@@ -29,7 +32,16 @@
 namespace rgb {
 
 constexpr int kRowbalThreads = 256;
-constexpr int kRowbalUnroll = 8;
+constexpr int kRowbalSmem = 0;  // dynamic shared memory per CTA
+
+// Streaming knobs (measured on B200; see the tuning notes in DESIGN.md):
+// U rows per register batch, DB = keep a second batch in flight while
+// folding, MINB = minimum resident CTAs per SM requested from ptxas.
+struct RowbalTuning {
+  static constexpr int kUnroll = 4;
+  static constexpr bool kDoubleBuffer = false;
+  static constexpr int kMinBlocks = 3;
+};
 constexpr int kSumBlock = 8;  // rows summed plainly before a compensated add
 
 // Piece slot kinds in the unit metadata.
@@ -159,13 +171,13 @@ __device__ int64_t path_search(const OffT *offsets, int64_t b, int64_t diag, int
   return lo;
 }
 
-template <typename T, typename OffT, int OP, int VEC>
-__global__ void __launch_bounds__(kRowbalThreads)
+template <typename T, typename OffT, int OP, int VEC, int U = RowbalTuning::kUnroll,
+          bool DB = RowbalTuning::kDoubleBuffer, int MINB = RowbalTuning::kMinBlocks>
+__global__ void __launch_bounds__(kRowbalThreads, MINB)
 rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
               int64_t n, int64_t b, int64_t d, int g_shift, int vec_cols, int64_t units,
               float *__restrict__ pieces, UnitMeta *__restrict__ meta) {
   using Acc = RowAcc<OP, VEC>;
-  constexpr int U = kRowbalUnroll;
   const int lane = threadIdx.x & 31;
   const int G = 1 << g_shift;
   const int q = lane >> g_shift;          // unit within the warp
@@ -173,8 +185,8 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   const int group_base = q << g_shift;
   const unsigned group_mask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << group_base);
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g_shift);
-  const int64_t unit = static_cast<int64_t>(blockIdx.x) * units_per_cta + (threadIdx.x >> 5) * (32 >> g_shift) + q;
-  if (unit >= units) return;  // whole groups exit together
+  const int unit_in_cta = (threadIdx.x >> 5) * (32 >> g_shift) + q;
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * units_per_cta + unit_in_cta;  // < units by construction
   const int cv = blockIdx.y * 32 + gl;
   const bool active = cv < vec_cols;
   const int64_t col = static_cast<int64_t>(cv) * VEC;
@@ -202,16 +214,22 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   bool first = true;
   const bool first_started_here = seg < b ? load_offset(offsets, seg) >= j0 : true;
 
-  float *const unit_pieces = pieces + unit * 2 * Acc::kWidth * d;  // [2][kWidth][d]
-  const int64_t stride = d;                                          // between s and c
+  // Unit pieces stay in shared memory: slot 0 = HEAD, slot 1 = TAIL or
+  // THROUGH, VEC * kWidth floats per lane; the unit's metadata beside them.
+  constexpr int W = Acc::kWidth;
+  __shared__ float s_piece[2][kRowbalThreads * VEC * W];
+  __shared__ int64_t s_head[kRowbalThreads], s_tail[kRowbalThreads];
+  __shared__ int32_t s_kind[kRowbalThreads];
+  float *const my_head = &s_piece[0][threadIdx.x * VEC * W];
+  float *const my_tail = &s_piece[1][threadIdx.x * VEC * W];
   Acc acc;
   acc.init();
 
   // Finalise `seg` (its end is consumed by this unit).
   auto finish = [&]() {
     if (first && !first_started_here) {
-      if (active) acc.store_piece(unit_pieces + col, stride);
-      if (blockIdx.y == 0 && gl == 0) meta[unit].head_seg = seg;
+      acc.store_piece(my_head, VEC);
+      if (gl == 0) s_head[unit_in_cta] = seg;
     } else if (active) {
       float y[VEC];
       acc.value(y);
@@ -223,28 +241,58 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
     next_b = seg < b ? end_of(seg) : INT64_MAX;
   };
 
-  if (blockIdx.y == 0 && gl == 0) {
-    meta[unit].head_seg = -1;
-    meta[unit].tail_seg = -1;
-    meta[unit].tail_kind = PIECE_NONE;
+  if (gl == 0) {
+    s_head[unit_in_cta] = -1;
+    s_tail[unit_in_cta] = -1;
+    s_kind[unit_in_cta] = PIECE_NONE;
   }
 
-  for (int64_t r = j0; r < j1; r += U) {
-    // Issue U row loads of this unit's stream, then fold them in order.
-    typename VecIO<T, VEC>::Raw raw[U];
-    const T *row_ptr = values + r * d + col;
+  // Register batches of U rows.  With DB a second batch is in flight while
+  // one is folded, so a warp always has loads pending.  A batch without a
+  // segment boundary takes the fast path (no per-row boundary test).
+  using Raw = typename VecIO<T, VEC>::Raw;
+  const T *ptr = values + j0 * d + col;
+  auto load_batch = [&](Raw (&raw)[U], int64_t rel) {  // rows j0 + rel .. + U
 #pragma unroll
-    for (int t = 0; t < U; ++t) {
-      if (active && r + t < j1) raw[t] = VecIO<T, VEC>::load_raw(row_ptr + t * d);
-    }
+    for (int t = 0; t < U; ++t)
+      if (active && j0 + rel + t < j1) raw[t] = VecIO<T, VEC>::load_raw(ptr + (rel + t) * d);
+  };
+  auto fold_batch = [&](const Raw (&raw)[U], int64_t r) {
+    if (r + U <= j1 && next_b >= r + U) {
 #pragma unroll
-    for (int t = 0; t < U; ++t) {
-      if (r + t < j1) {
-        while (next_b <= r + t) finish();  // segments ending before this row (incl. empty ones)
+      for (int t = 0; t < U; ++t) {
         float x[VEC];
         VecIO<T, VEC>::unpack(raw[t], x);
         acc.fold(x);
       }
+    } else {
+#pragma unroll
+      for (int t = 0; t < U; ++t) {
+        if (r + t < j1) {
+          while (next_b <= r + t) finish();  // segments ending before this row (incl. empty ones)
+          float x[VEC];
+          VecIO<T, VEC>::unpack(raw[t], x);
+          acc.fold(x);
+        }
+      }
+    }
+  };
+  if constexpr (DB) {
+    Raw ra[U], rb[U];
+    load_batch(ra, 0);
+    load_batch(rb, U);
+    for (int64_t rel = 0; j0 + rel < j1; rel += 2 * U) {
+      fold_batch(ra, j0 + rel);
+      load_batch(ra, rel + 2 * U);
+      if (j0 + rel + U >= j1) break;
+      fold_batch(rb, j0 + rel + U);
+      load_batch(rb, rel + 3 * U);
+    }
+  } else {
+    for (int64_t rel = 0; j0 + rel < j1; rel += U) {
+      Raw ra[U];
+      load_batch(ra, rel);
+      fold_batch(ra, j0 + rel);
     }
   }
   while (seg < i1) finish();  // ends consumed after the last row
@@ -253,50 +301,146 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   if (seg < b) {
     const int64_t start = load_offset(offsets, seg);
     if ((start > j0 ? start : j0) < j1) {
-      if (active) acc.store_piece(unit_pieces + Acc::kWidth * d + col, stride);
-      if (blockIdx.y == 0 && gl == 0) {
-        meta[unit].tail_seg = seg;
-        meta[unit].tail_kind = start < j0 ? PIECE_THROUGH : PIECE_TAIL;
+      acc.store_piece(my_tail, VEC);
+      if (gl == 0) {
+        s_tail[unit_in_cta] = seg;
+        s_kind[unit_in_cta] = start < j0 ? PIECE_THROUGH : PIECE_TAIL;
       }
+    }
+  }
+  __syncthreads();
+
+  // Combine the CTA's unit pieces in row order (one thread per column lane):
+  // a segment whose TAIL, THROUGH and HEAD pieces all lie in this CTA is
+  // finished here; what remains is at most one CTA-level HEAD (a segment
+  // open at the CTA's start that ends in it) and one TAIL / THROUGH (open
+  // at its end), written to global memory for the fix-up.
+  if (threadIdx.x < G) {
+    const int c_lane = threadIdx.x;
+    const int c_cv = blockIdx.y * 32 + c_lane;
+    const bool c_active = c_cv < vec_cols;
+    const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
+    float *const cta_pieces = pieces + static_cast<int64_t>(blockIdx.x) * 2 * W * d;
+    Acc carry;
+    carry.init();
+    bool have = false, here = false;
+    int64_t carry_seg = -1, cta_head = -1;
+    for (int k = 0; k < units_per_cta; ++k) {
+      const int slot = (k << g_shift) + c_lane;
+      const int64_t h = s_head[k];
+      if (h >= 0) {
+        if (have && carry_seg == h) {
+          carry.merge_piece(&s_piece[0][slot * VEC * W], VEC);
+        } else {
+          carry.load_piece(&s_piece[0][slot * VEC * W], VEC);
+          here = false;
+        }
+        if (here) {
+          if (c_active) {
+            float y[VEC];
+            carry.value(y);
+            VecIO<T, VEC>::store(out + h * d + c_col, y);
+          }
+        } else {
+          if (c_active) carry.store_piece(cta_pieces + c_col, d);
+          cta_head = h;
+        }
+        have = false;
+      }
+      const int kind = s_kind[k];
+      if (kind == PIECE_TAIL) {
+        carry.load_piece(&s_piece[1][slot * VEC * W], VEC);
+        have = true;
+        here = true;
+        carry_seg = s_tail[k];
+      } else if (kind == PIECE_THROUGH) {
+        if (have && carry_seg == s_tail[k]) {
+          carry.merge_piece(&s_piece[1][slot * VEC * W], VEC);
+        } else {
+          carry.load_piece(&s_piece[1][slot * VEC * W], VEC);
+          have = true;
+          here = false;
+          carry_seg = s_tail[k];
+        }
+      }
+    }
+    if (have && c_active) carry.store_piece(cta_pieces + W * d + c_col, d);
+    if (blockIdx.y == 0 && c_lane == 0) {
+      meta[blockIdx.x].head_seg = cta_head;
+      meta[blockIdx.x].tail_seg = have ? carry_seg : -1;
+      meta[blockIdx.x].tail_kind = have ? (here ? PIECE_TAIL : PIECE_THROUGH) : PIECE_NONE;
     }
   }
 }
 
-// Merge the pieces of every segment cut by unit boundaries.  One warp per
-// (owner unit, column tile): the owner is the unit where the segment
-// starts; it walks the following units' THROUGH pieces and ends at the
-// HEAD piece of the unit that consumed the segment's end.
+// Merge the pieces of every segment cut by CTA boundaries.  One CTA of
+// kFixupThreads per (owner, column tile): the owner is the main kernel's
+// CTA where the segment starts (its TAIL piece).  The fix-up CTA first
+// finds the chain's end -- the CTA holding the HEAD piece -- scanning
+// kFixupThreads metadata entries per step, then its warps merge contiguous
+// runs of the THROUGH pieces between in parallel, and warp 0 merges TAIL,
+// the warps' partials (in order) and HEAD.  The merge tree depends only on
+// the chain, so results are deterministic.
+constexpr int kFixupThreads = 256;
+
 template <typename T, int OP, int VEC>
-__global__ void __launch_bounds__(32)
+__global__ void __launch_bounds__(kFixupThreads)
 rowbal_fixup_kernel(T *__restrict__ out, int64_t d, int vec_cols, int64_t units,
                     const float *__restrict__ pieces, const UnitMeta *__restrict__ meta) {
   using Acc = RowAcc<OP, VEC>;
+  constexpr int NW = kFixupThreads / 32;
   const int64_t u = blockIdx.x;
-  if (meta[u].tail_kind != PIECE_TAIL) return;
+  if (meta[u].tail_kind != PIECE_TAIL) return;  // uniform across the CTA
   const int64_t seg = meta[u].tail_seg;
-  const int cv = blockIdx.y * 32 + threadIdx.x;
-  if (cv >= vec_cols) return;
+  __shared__ int64_t s_end;
+  __shared__ float s_part[NW][2][32 * VEC];  // per-warp partials: (s, c) or (m)
+  if (threadIdx.x == 0) s_end = INT64_MAX;
+  __syncthreads();
+  for (int64_t base = u + 1; base < units; base += kFixupThreads) {
+    const int64_t v = base + threadIdx.x;
+    if (v < units && meta[v].head_seg == seg) atomicMin(reinterpret_cast<unsigned long long *>(&s_end),
+                                                        static_cast<unsigned long long>(v));
+    __syncthreads();
+    if (s_end != INT64_MAX) break;  // uniform: read after the barrier
+    __syncthreads();
+  }
+  const int64_t end = s_end;  // the HEAD unit: the segment's end is consumed by a later unit
+  if (end >= units) return;   // unreachable for valid offsets; never read past the metadata
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cv = blockIdx.y * 32 + lane;
+  const bool active = cv < vec_cols;
   const int64_t col = static_cast<int64_t>(cv) * VEC;
   const int64_t stride = d;
-  const int64_t piece_span = 2 * Acc::kWidth * d;
+  const int64_t span = 2 * Acc::kWidth * d;
+  // THROUGH pieces of CTAs (u, end): warp w takes a contiguous run, four
+  // entries per step with independent loads.
+  const int64_t first = u + 1, count = end > first ? end - first : 0;
+  const int64_t per = (count + NW - 1) / NW;
+  const int64_t lo = first + warp * per, hi = lo + per < end ? lo + per : end;
   Acc acc;
-  acc.load_piece(pieces + u * piece_span + Acc::kWidth * d + col, stride);
-  for (int64_t v = u + 1; v < units; ++v) {
-    const UnitMeta m = meta[v];
-    if (m.head_seg < 0 && m.tail_seg < 0) continue;  // a unit with an empty slice of the path
-    if (m.head_seg == seg) {
-      acc.merge_piece(pieces + v * piece_span + col, stride);
-      break;
+  acc.init();
+  if (active) {
+    for (int64_t v = lo; v < hi; v += 4) {
+      int32_t kind[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) kind[i] = v + i < hi ? meta[v + i].tail_kind : PIECE_NONE;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (kind[i] == PIECE_THROUGH) acc.merge_piece(pieces + (v + i) * span + Acc::kWidth * d + col, stride);
     }
-    if (m.tail_seg == seg && m.tail_kind == PIECE_THROUGH) {
-      acc.merge_piece(pieces + v * piece_span + Acc::kWidth * d + col, stride);
-      continue;
-    }
-    break;
   }
-  float y[VEC];
-  acc.value(y);
-  VecIO<T, VEC>::store(out + seg * d + col, y);
+  if (active) acc.store_piece(&s_part[warp][0][lane * VEC], 32 * VEC);
+  __syncthreads();
+  if (warp == 0 && active) {
+    Acc total;
+    total.load_piece(pieces + u * span + Acc::kWidth * d + col, stride);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) total.merge_piece(&s_part[w][0][lane * VEC], 32 * VEC);
+    total.merge_piece(pieces + end * span + col, stride);
+    float y[VEC];
+    total.value(y);
+    VecIO<T, VEC>::store(out + seg * d + col, y);
+  }
 }
 
 }  // namespace rgb
