@@ -51,6 +51,7 @@ enum KernelId : int {
   K_ROWBAL = 5,
   K_ROWBAL_FIXUP = 6,
   K_SHARD_COMBINE = 7,
+  K_ROWBAL_PACKED = 8,
 };
 
 // Recording helper for rg_report.

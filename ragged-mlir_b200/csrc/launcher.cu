@@ -187,6 +187,7 @@ const char *rg_kernel_name(int kernel_id) {
     case K_ROWBAL: return "rowbalanced";
     case K_ROWBAL_FIXUP: return "rowbalanced_fixup";
     case K_SHARD_COMBINE: return "shard_combine";
+    case K_ROWBAL_PACKED: return "rowbalanced_packed";
   }
   return "";
 }

@@ -37,6 +37,21 @@ const void *kernel_ptr() {
   return reinterpret_cast<const void *>(&rowbal_kernel<T, OffT, OP, VEC>);
 }
 
+// Narrow rows that pack whole rows into 16-byte packets (2, 4 or 8 bytes a
+// row) take the packed kernel; VEC equals D for them.
+bool packs(const Problem &p, const Geometry &g) {
+  const int64_t row_bytes = p.d * elem_bytes(p.dtype);
+  return !(p.flags & RG_FLAG_NO_VECTORIZE) && row_bytes < 16 && 16 % row_bytes == 0 && g.vec == p.d;
+}
+
+template <typename T, typename OffT, int OP, int VEC>
+const void *packed_ptr() {
+  if constexpr (VEC * sizeof(T) < 16) {
+    return reinterpret_cast<const void *>(&rowbal_packed_kernel<T, OffT, OP, VEC>);
+  }
+  return nullptr;
+}
+
 constexpr int64_t kAlign = 256;
 int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -48,13 +63,19 @@ struct Plan {
 
 // Units: enough CTAs for one resident wave (per column tile), but no more
 // than one unit per 64 path items.
-int make_plan(const Problem &p, const Geometry &g, const void *kernel, Plan *plan) {
+int make_plan(const Problem &p, const Geometry &g, const void *kernel, const void *packed, Plan *plan) {
   DeviceProps dev;
   int status = device_props(&dev);
   if (status) return status;
   int per_sm = 0;
   status = occupancy(kernel, dev.device, kRowbalThreads, &per_sm);
   if (status) return status;
+  if (packed) {  // size the plan for whichever kernel the call may take
+    int packed_per_sm = 0;
+    status = occupancy(packed, dev.device, kRowbalThreads, &packed_per_sm);
+    if (status) return status;
+    if (packed_per_sm > per_sm) per_sm = packed_per_sm;
+  }
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
   int64_t ctas = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
   if (ctas < 1) ctas = 1;
@@ -73,7 +94,8 @@ template <typename T, typename OffT, int OP, int VEC>
 int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *bytes, cudaStream_t stream,
               rg_report *report) {
   Plan plan;
-  int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC>(), &plan);
+  const void *packed = packs(p, g) ? packed_ptr<T, OffT, OP, VEC>() : nullptr;
+  int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC>(), packed, &plan);
   if (status) return status;
   if (bytes) {
     *bytes = plan.pieces_bytes + plan.meta_bytes;
@@ -81,6 +103,35 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   }
   float *pieces = static_cast<float *>(workspace);
   UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
+  if constexpr (VEC * sizeof(T) < 16) {
+    if (packed && reinterpret_cast<uintptr_t>(p.values) % 16 == 0) {
+      dim3 grid(plan.ctas, 1, 1);
+      rowbal_packed_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, 0, stream>>>(
+          static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
+          plan.units, pieces, meta);
+      record_launch(report, K_ROWBAL_PACKED, grid, kRowbalThreads, 0);
+      status = check_cuda(cudaGetLastError(), "rowbal_packed_kernel launch");
+      if (status || plan.ctas < 2) return status;
+      dim3 fix_grid(static_cast<unsigned>(plan.ctas), 1, 1);
+      rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d,
+                                                                              g.vec_cols, plan.ctas, pieces, meta);
+      record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
+      return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
+    }
+  }
+  int64_t ctas = plan.ctas;  // the unpacked kernel may hold fewer CTAs than the plan sized for
+  {
+    DeviceProps dev;
+    status = device_props(&dev);
+    if (status) return status;
+    int per_sm = 0;
+    status = occupancy(kernel_ptr<T, OffT, OP, VEC>(), dev.device, kRowbalThreads, &per_sm);
+    if (status) return status;
+    const int64_t cap = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
+    if (ctas > cap && cap >= 1) ctas = cap;
+  }
+  plan.ctas = static_cast<int>(ctas);
+  plan.units = ctas * ((kRowbalThreads / 32) << (5 - g.g_shift));
   dim3 grid(plan.ctas, g.col_tiles, 1);
   rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,

@@ -171,6 +171,69 @@ __device__ int64_t path_search(const OffT *offsets, int64_t b, int64_t diag, int
   return lo;
 }
 
+// Combine `count` consecutive units' pieces in row order, for one column
+// lane.  piece(k, slot) points at unit k's slot (0 = HEAD, 1 = TAIL or
+// THROUGH) for this lane, `pstride` floats between its s and c halves.  A
+// segment whose pieces all lie among these units is finished and stored to
+// out (when `active`); the remaining HEAD and TAIL / THROUGH pieces go to
+// head_dst / tail_dst (`dstride` between halves) and, if `m` is not null,
+// their segments and kind to *m.
+template <typename T, int OP, int VEC, typename PieceFn>
+__device__ __forceinline__ void combine_pieces(int count, PieceFn piece, int pstride, const int64_t *heads,
+                                               const int64_t *tails, const int32_t *kinds, bool active, T *out,
+                                               int64_t d, int64_t col, float *head_dst, float *tail_dst,
+                                               int64_t dstride, UnitMeta *m) {
+  using Acc = RowAcc<OP, VEC>;
+  Acc carry;
+  carry.init();
+  bool have = false, here = false;
+  int64_t carry_seg = -1, head_seg = -1;
+  for (int k = 0; k < count; ++k) {
+    const int64_t h = heads[k];
+    if (h >= 0) {
+      if (have && carry_seg == h) {
+        carry.merge_piece(piece(k, 0), pstride);
+      } else {
+        carry.load_piece(piece(k, 0), pstride);
+        here = false;
+      }
+      if (here) {
+        if (active) {
+          float y[VEC];
+          carry.value(y);
+          VecIO<T, VEC>::store(out + h * d + col, y);
+        }
+      } else {
+        if (active) carry.store_piece(head_dst, dstride);
+        head_seg = h;
+      }
+      have = false;
+    }
+    const int kind = kinds[k];
+    if (kind == PIECE_TAIL) {
+      carry.load_piece(piece(k, 1), pstride);
+      have = true;
+      here = true;
+      carry_seg = tails[k];
+    } else if (kind == PIECE_THROUGH) {
+      if (have && carry_seg == tails[k]) {
+        carry.merge_piece(piece(k, 1), pstride);
+      } else {
+        carry.load_piece(piece(k, 1), pstride);
+        have = true;
+        here = false;
+        carry_seg = tails[k];
+      }
+    }
+  }
+  if (have && active) carry.store_piece(tail_dst, dstride);
+  if (m) {
+    m->head_seg = head_seg;
+    m->tail_seg = have ? carry_seg : -1;
+    m->tail_kind = have ? (here ? PIECE_TAIL : PIECE_THROUGH) : PIECE_NONE;
+  }
+}
+
 template <typename T, typename OffT, int OP, int VEC, int U = RowbalTuning::kUnroll,
           bool DB = RowbalTuning::kDoubleBuffer, int MINB = RowbalTuning::kMinBlocks>
 __global__ void __launch_bounds__(kRowbalThreads, MINB)
@@ -318,58 +381,157 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   if (threadIdx.x < G) {
     const int c_lane = threadIdx.x;
     const int c_cv = blockIdx.y * 32 + c_lane;
-    const bool c_active = c_cv < vec_cols;
-    const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
     float *const cta_pieces = pieces + static_cast<int64_t>(blockIdx.x) * 2 * W * d;
-    Acc carry;
-    carry.init();
-    bool have = false, here = false;
-    int64_t carry_seg = -1, cta_head = -1;
-    for (int k = 0; k < units_per_cta; ++k) {
-      const int slot = (k << g_shift) + c_lane;
-      const int64_t h = s_head[k];
-      if (h >= 0) {
-        if (have && carry_seg == h) {
-          carry.merge_piece(&s_piece[0][slot * VEC * W], VEC);
+    const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
+    auto piece = [&](int k, int slot) { return &s_piece[slot][((k << g_shift) + c_lane) * VEC * W]; };
+    combine_pieces<T, OP, VEC>(units_per_cta, piece, VEC, s_head, s_tail, s_kind, c_cv < vec_cols, out, d, c_col,
+                               cta_pieces + c_col, cta_pieces + W * d + c_col, d,
+                               blockIdx.y == 0 && c_lane == 0 ? &meta[blockIdx.x] : nullptr);
+  }
+}
+
+// Narrow rows (D * sizeof(T) in {2, 4, 8} bytes): every lane is a unit and
+// reads 16-byte packets of R = 16 / (D * sizeof(T)) whole rows, folding a
+// packet at once when no segment boundary falls inside it.  A warp finds
+// its slice of the merge path with a 32-ary search; each lane then finds
+// its own slice by binary search inside the warp's segment range.  The next
+// four segment ends sit in a register window that is refilled one entry
+// per finished segment, so short segments do not wait on offsets loads.
+// Pieces are combined per warp (lane 0 over 32 units) and then per CTA
+// (thread 0 over the 8 warps), leaving one HEAD and one TAIL / THROUGH per
+// CTA for the fix-up kernel.
+
+// First k in [lo, hi] with offsets[k+1] + k >= diag, for one thread.
+template <typename OffT>
+__device__ __forceinline__ int64_t path_search_range(const OffT *offsets, int64_t lo, int64_t hi, int64_t diag) {
+  while (lo < hi) {
+    const int64_t mid = lo + (hi - lo) / 2;
+    if (load_offset(offsets, mid + 1) + mid >= diag) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+template <typename T, typename OffT, int OP, int DS, int U = 4, int MINB = 3>
+__global__ void __launch_bounds__(kRowbalThreads, MINB)
+rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
+                     int64_t n, int64_t b, int64_t units, float *__restrict__ pieces, UnitMeta *__restrict__ meta) {
+  using Acc = RowAcc<OP, DS>;
+  constexpr int W = Acc::kWidth;
+  constexpr int R = 16 / (DS * static_cast<int>(sizeof(T)));  // rows per 16-byte packet
+  constexpr int NW = kRowbalThreads / 32;
+  constexpr int E = 16 / static_cast<int>(sizeof(T));         // elements per packet
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t path = n + b;
+  auto diag_of = [&](int64_t u) { return path / units * u + (u < path % units ? u : path % units); };
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * kRowbalThreads + threadIdx.x;
+  const int64_t warp_unit = unit - lane;
+  const int64_t wi0 = path_search(offsets, b, diag_of(warp_unit), 32, lane, 0xffffffffu, 0);
+  const int64_t wi1 = path_search(offsets, b, diag_of(warp_unit + 32), 32, lane, 0xffffffffu, 0);
+  const int64_t d0 = diag_of(unit), d1 = diag_of(unit + 1);
+  const int64_t i0 = path_search_range(offsets, wi0, wi1, d0);
+  const int64_t i1 = path_search_range(offsets, i0, wi1, d1);
+  const int64_t j0 = d0 - i0, j1 = d1 - i1;
+
+  __shared__ float s_piece[2][kRowbalThreads * DS * W];
+  __shared__ int64_t s_head[kRowbalThreads], s_tail[kRowbalThreads];
+  __shared__ int32_t s_kind[kRowbalThreads];
+  __shared__ float w_piece[2][NW * DS * W];
+  __shared__ int64_t w_head[NW], w_tail[NW];
+  __shared__ int32_t w_kind[NW];
+  float *const my_head = &s_piece[0][threadIdx.x * DS * W];
+  float *const my_tail = &s_piece[1][threadIdx.x * DS * W];
+  s_head[threadIdx.x] = -1;
+  s_tail[threadIdx.x] = -1;
+  s_kind[threadIdx.x] = PIECE_NONE;
+
+  int64_t seg = i0;
+  auto end_at = [&](int64_t s1) -> int64_t { return s1 <= b ? load_offset(offsets, s1) : INT64_MAX; };
+  int64_t w0 = end_at(seg + 1), w1 = end_at(seg + 2), w2 = end_at(seg + 3), w3 = end_at(seg + 4);
+  bool first = true;
+  const bool first_started_here = seg < b ? load_offset(offsets, seg) >= j0 : true;
+  Acc acc;
+  acc.init();
+  auto finish = [&]() {
+    if (first && !first_started_here) {
+      acc.store_piece(my_head, DS);
+      s_head[threadIdx.x] = seg;
+    } else {
+      float y[DS];
+      acc.value(y);
+      VecIO<T, DS>::store(out + seg * DS, y);
+    }
+    first = false;
+    acc.init();
+    ++seg;
+    w0 = w1;
+    w1 = w2;
+    w2 = w3;
+    w3 = end_at(seg + 4);
+  };
+  auto fold_row = [&](const float (&x)[E], int k) {
+    float row[DS];
+#pragma unroll
+    for (int f = 0; f < DS; ++f) row[f] = x[k * DS + f];
+    acc.fold(row);
+  };
+
+  const uint4 *packets = reinterpret_cast<const uint4 *>(values);
+  const int64_t p_begin = j0 / R, p_end = (j1 + R - 1) / R;
+  for (int64_t p = p_begin; p < p_end; p += U) {
+    uint4 raw[U];
+#pragma unroll
+    for (int t = 0; t < U; ++t)
+      if (p + t < p_end) raw[t] = __ldg(packets + p + t);
+#pragma unroll
+    for (int t = 0; t < U; ++t) {
+      if (p + t < p_end) {
+        float x[E];
+        VecIO<T, E>::unpack(*reinterpret_cast<const typename VecIO<T, E>::Raw *>(&raw[t]), x);
+        const int64_t r0 = (p + t) * R;
+        if (r0 >= j0 && r0 + R <= j1 && w0 >= r0 + R) {
+#pragma unroll
+          for (int k = 0; k < R; ++k) fold_row(x, k);
         } else {
-          carry.load_piece(&s_piece[0][slot * VEC * W], VEC);
-          here = false;
-        }
-        if (here) {
-          if (c_active) {
-            float y[VEC];
-            carry.value(y);
-            VecIO<T, VEC>::store(out + h * d + c_col, y);
+#pragma unroll
+          for (int k = 0; k < R; ++k) {
+            const int64_t r = r0 + k;
+            if (r >= j0 && r < j1) {
+              while (w0 <= r) finish();
+              fold_row(x, k);
+            }
           }
-        } else {
-          if (c_active) carry.store_piece(cta_pieces + c_col, d);
-          cta_head = h;
-        }
-        have = false;
-      }
-      const int kind = s_kind[k];
-      if (kind == PIECE_TAIL) {
-        carry.load_piece(&s_piece[1][slot * VEC * W], VEC);
-        have = true;
-        here = true;
-        carry_seg = s_tail[k];
-      } else if (kind == PIECE_THROUGH) {
-        if (have && carry_seg == s_tail[k]) {
-          carry.merge_piece(&s_piece[1][slot * VEC * W], VEC);
-        } else {
-          carry.load_piece(&s_piece[1][slot * VEC * W], VEC);
-          have = true;
-          here = false;
-          carry_seg = s_tail[k];
         }
       }
     }
-    if (have && c_active) carry.store_piece(cta_pieces + W * d + c_col, d);
-    if (blockIdx.y == 0 && c_lane == 0) {
-      meta[blockIdx.x].head_seg = cta_head;
-      meta[blockIdx.x].tail_seg = have ? carry_seg : -1;
-      meta[blockIdx.x].tail_kind = have ? (here ? PIECE_TAIL : PIECE_THROUGH) : PIECE_NONE;
+  }
+  while (seg < i1) finish();
+  if (seg < b) {
+    const int64_t start = load_offset(offsets, seg);
+    if ((start > j0 ? start : j0) < j1) {
+      acc.store_piece(my_tail, DS);
+      s_tail[threadIdx.x] = seg;
+      s_kind[threadIdx.x] = start < j0 ? PIECE_THROUGH : PIECE_TAIL;
     }
+  }
+  __syncwarp();
+  // Level 1: lane 0 of each warp combines its 32 units.
+  if (lane == 0) {
+    const int base = warp * 32;
+    auto piece = [&](int k, int slot) { return &s_piece[slot][(base + k) * DS * W]; };
+    UnitMeta m;
+    combine_pieces<T, OP, DS>(32, piece, DS, s_head + base, s_tail + base, s_kind + base, true, out, DS, 0,
+                              &w_piece[0][warp * DS * W], &w_piece[1][warp * DS * W], DS, &m);
+    w_head[warp] = m.head_seg;
+    w_tail[warp] = m.tail_seg;
+    w_kind[warp] = m.tail_kind;
+  }
+  __syncthreads();
+  // Level 2: thread 0 combines the warps into the CTA's pieces.
+  if (threadIdx.x == 0) {
+    auto piece = [&](int k, int slot) { return &w_piece[slot][k * DS * W]; };
+    float *const cta_pieces = pieces + static_cast<int64_t>(blockIdx.x) * 2 * W * DS;
+    combine_pieces<T, OP, DS>(NW, piece, DS, w_head, w_tail, w_kind, true, out, DS, 0, cta_pieces,
+                              cta_pieces + W * DS, DS, &meta[blockIdx.x]);
   }
 }
 

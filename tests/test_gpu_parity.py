@@ -212,3 +212,32 @@ def test_validation_errors(cuda):
         prog.run(values, offsets, values[:1])
     with pytest.raises(RuntimeUnavailable, match="checked"):
         prog.run(values, offsets, torch.empty((1, 4), device="cuda"), mode="checked")
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("dtype,d", [("f32", 1), ("f32", 2), ("bf16", 1), ("bf16", 2), ("bf16", 4)])
+def test_narrow_rows_packed_and_unaligned(cuda, op, dtype, d):
+    """Rows of 2-8 bytes: the packed kernel (16-byte aligned values) and
+    the per-row kernel it falls back to for a view that is not."""
+    torch = cuda
+    from helpers import program
+    lengths = make_lengths("bimodal", 500, 20_000, seed=23)
+    lengths[3] = 0
+    offsets = offsets_of(lengths, "i32")
+    values = prepared(np.random.default_rng(24).normal(size=(int(offsets[-1]), d)), dtype)
+    tdtype = torch.float32 if dtype == "f32" else torch.bfloat16
+    prog = program(op, dtype, d, "i32")
+    device_offsets = torch.from_numpy(offsets).to("cuda")
+    for shift in (0, 1):  # shift one row: misaligns the base for the packed loads
+        base = torch.zeros((values.shape[0] + 1, d), dtype=tdtype, device="cuda")
+        view = base[shift:shift + values.shape[0]]
+        view.copy_(torch.from_numpy(values).to(tdtype))
+        out = torch.empty((offsets.size - 1, d), dtype=tdtype, device="cuda")
+        report = prog.run(view, device_offsets, out, select="rowbalanced")
+        torch.cuda.synchronize()
+        check(out.float().cpu().numpy().astype(np.float64), values, offsets, op, dtype)
+        names = set(report.kernel_names)
+        if shift == 0:
+            assert "rowbalanced_packed" in names
+        else:
+            assert "rowbalanced" in names and "rowbalanced_packed" not in names
