@@ -76,6 +76,7 @@ typedef struct rg_report {
   int32_t d_tile;                         /* threads spanning one row tile    */
   int32_t streams;                        /* streams used (1: caller's only)  */
   int64_t workspace_bytes;                /* scratch the call required        */
+  int64_t thresholds[2];                  /* classified: warp- and CTA-class length bounds (rows) */
 } rg_report;
 
 typedef struct rg_device_info {

@@ -68,19 +68,69 @@ __device__ __forceinline__ float kahan_value(float s, float c) {
   return is_finite(s) ? __fsub_rn(s, c) : s;
 }
 
-// exp for the softmax statistics and output.  CUDA's expf (accurate to a
-// couple of ulp over the whole range) is called, never restated.
-__device__ __forceinline__ float exp_f(float x) { return expf(x); }
+// e^t for the softmax statistics and output, as 2^(t * log2 e) on the SFU
+// (PTX ex2.approx.ftz.f32: about 2 ulp; results below 2^-126 flush to +0).
+// t = x - r is rounded once and the product once, so a term e^t carries a
+// relative error of about |t| * 2^-23: under 1e-5 for every term the f32
+// softmax tolerance (|a - ref| <= 1e-5 |ref| + FLT_MIN) does not already
+// absorb.  One SFU instruction and two FMA-pipe instructions per term keep
+// the D=128 bf16 softmax below the HBM time on B200.
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float exp2_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float exp_diff(float x, float r) { return exp2_sfu(__fmul_rn(__fsub_rn(x, r), kLog2e)); }
+
+// Packed pairs on sm_100's two-wide FP32 pipe (add/sub/mul.rn.f32x2): one
+// instruction per two lanes' worth of work, each half rounded exactly as
+// the scalar __fadd_rn / __fsub_rn / __fmul_rn.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long add2_rn(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long sub2_rn(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long mul2_rn(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// e^(x - r) for two features at once: the packed subtraction and scaling,
+// then one SFU exponential per half (same rounding as exp_diff).
+__device__ __forceinline__ unsigned long long exp_diff2(unsigned long long x, unsigned long long r) {
+  const unsigned long long t = mul2_rn(sub2_rn(x, r), pack2(kLog2e, kLog2e));
+  float lo, hi;
+  unpack2(t, lo, hi);
+  return pack2(exp2_sfu(lo), exp2_sfu(hi));
+}
 
 // --------------------------------------------------- online softmax stats --
 //
 // State per feature: reference r, compensated mass (s, c) relative to r.
 // A batch of values with batch maximum bm is folded as in the reference:
 // the reference recentres only when it is empty (-inf), unordered (NaN) or
-// when the maximum exceeds it by more than one, so every mass stays below
+// when the maximum exceeds it by more than one, so every term stays below
 // e and earlier rounding errors are damped by each rescale.  A +inf anchor
 // makes the column NaN; a -inf anchor means every value so far was -inf and
-// adds no mass.
+// adds no mass.  The batch's terms are summed plainly (each is at most e)
+// and the batch total is added with compensation.
 
 struct Stats {
   float r, s, c;
@@ -99,26 +149,26 @@ __device__ __forceinline__ void stats_fold(Stats &st, const float (&x)[COUNT]) {
   const bool empty = st.r == -kInf;
   const bool unordered = (st.r != st.r) || (bm != bm);
   const bool advance = __fsub_rn(m, st.r) > 1.0f;
-  const float anchor = (empty || unordered || advance) ? m : st.r;
-  if (anchor != st.r) {
+  if (empty || unordered || advance) {
     if (empty) {
       st.s = 0.0f;
       st.c = 0.0f;
     } else {
-      const float scale = exp_f(__fsub_rn(st.r, anchor));
+      const float scale = exp_diff(st.r, m);
       st.s = __fmul_rn(st.s, scale);
       st.c = __fmul_rn(st.c, scale);
     }
-    st.r = anchor;
+    st.r = m;
+    if (m == kInf || m != m) {
+      st.s = __int_as_float(0x7fffffff);
+      st.c = 0.0f;
+    }
   }
-  if (anchor == kInf || anchor != anchor) {
-    st.s = __int_as_float(0x7fffffff);
-    st.c = 0.0f;
-    return;
-  }
-  if (anchor == -kInf) return;  // every value so far is -inf: no mass
+  if (st.r == -kInf || !is_finite(st.r)) return;  // no mass yet, or the column is already NaN
+  float p = exp_diff(x[0], st.r);
 #pragma unroll
-  for (int i = 0; i < COUNT; ++i) kahan_add_finite(st.s, st.c, exp_f(__fsub_rn(x[i], anchor)));
+  for (int i = 1; i < COUNT; ++i) p = __fadd_rn(p, exp_diff(x[i], st.r));
+  kahan_add_finite(st.s, st.c, p);
 }
 
 // Merge statistics b into a (ToGPU.cpp:486-508 `mergeStatistics`, with the
@@ -133,8 +183,7 @@ __device__ __forceinline__ void stats_merge(Stats &a, const Stats &b) {
   } else if (b.r == -kInf) {
     total = sa;
   } else {
-    total = __fadd_rn(__fmul_rn(sa, exp_f(__fsub_rn(a.r, m))),
-                      __fmul_rn(sb, exp_f(__fsub_rn(b.r, m))));
+    total = __fadd_rn(__fmul_rn(sa, exp_diff(a.r, m)), __fmul_rn(sb, exp_diff(b.r, m)));
   }
   if (m == kInf) total = __int_as_float(0x7fffffff);
   a.r = m;
@@ -142,9 +191,15 @@ __device__ __forceinline__ void stats_merge(Stats &a, const Stats &b) {
   a.c = 0.0f;
 }
 
-// Final normalisation of one value with the merged statistics.
-__device__ __forceinline__ float stats_normalize(float x, float r, float total) {
-  return __fdiv_rn(exp_f(__fsub_rn(x, r)), total);
+// Reciprocal of a column's total mass (once per column; IEEE rounded).
+__device__ __forceinline__ float stats_inverse(float total) { return __frcp_rn(total); }
+
+// Final normalisation of one value with the merged reference r and the
+// reciprocal of the total mass: e^(x - r) / total within 2 ulp + the term's
+// error.  NaN, +inf and all -inf columns come out NaN through the
+// arithmetic (NaN terms, NaN total, or 0 * inf).
+__device__ __forceinline__ float stats_normalize(float x, float r, float inv_total) {
+  return __fmul_rn(exp_diff(x, r), inv_total);
 }
 
 // ------------------------------------------------------------- vector I/O --
@@ -263,6 +318,63 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// ------------------------------------------------ bulk copies (TMA, 1-D) --
+//
+// cp.async.bulk moves a contiguous, 16-byte aligned block of global memory
+// (a multiple of 16 bytes) into this CTA's shared memory and signals an
+// mbarrier with the byte count: one instruction keeps tens of KB in flight.
+// No cluster multicast form is used anywhere in this library.
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make barrier initialisation and earlier generic-proxy shared-memory
+// accesses visible to the asynchronous (bulk copy) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// Arrive (count 1) and expect `bytes` of transactions on this phase.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_copy_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for phase `parity` of `bar` (each try_wait itself suspends
+// for a while); false after the limit, so a lost transaction cannot hang
+// the GPU.
+constexpr int kMbarWaitLimit = 1 << 22;
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  for (int i = 0; i < kMbarWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
 // ------------------------------------------------------------ accumulators --
 //
 // One accumulator per thread covers VEC adjacent features of one column.
@@ -280,6 +392,17 @@ struct Acc<OP_SUM, VEC> {
   __device__ __forceinline__ void fold(const float (&x)[VEC]) {
 #pragma unroll
     for (int v = 0; v < VEC; ++v) kahan_add(s[v], c[v], x[v]);
+  }
+  // U rows summed plainly, then added with compensation.
+  template <int U>
+  __device__ __forceinline__ void fold_batch(const float (&x)[U][VEC]) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      float p = x[0][v];
+#pragma unroll
+      for (int u = 1; u < U; ++u) p = __fadd_rn(p, x[u][v]);
+      kahan_add(s[v], c[v], p);
+    }
   }
   __device__ __forceinline__ void merge(const Acc &o) {
 #pragma unroll
@@ -310,6 +433,11 @@ struct Acc<OP_MAX, VEC> {
   __device__ __forceinline__ void fold(const float (&x)[VEC]) {
 #pragma unroll
     for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], x[v]);
+  }
+  template <int U>
+  __device__ __forceinline__ void fold_batch(const float (&x)[U][VEC]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) fold(x[u]);
   }
   __device__ __forceinline__ void merge(const Acc &o) {
 #pragma unroll

@@ -1,0 +1,250 @@
+// CTA- and warp-level segment reduction of the classified schedule.
+//
+// Geometry: G = 2^g_shift lanes cover one row tile (VEC features each), a
+// warp covers 32 / G rows per load, NW warps cover NW * 32 / G rows per
+// step.  Rows are strided across the "row lanes"; each thread folds its
+// rows into an Acc, row groups merge with xor shuffles and warps through
+// shared memory in a fixed order, so results are deterministic.
+//
+// Rows come from a "source": global memory (read-only path) or a block of
+// consecutive rows staged in shared memory by a bulk copy.  Both hand out
+// the raw vector of row r for this thread's column.
+#pragma once
+
+#include "common.cuh"
+
+namespace rgb {
+
+constexpr int kFoldUnroll = 4;
+
+template <typename T, int VEC>
+struct GlobalRows {
+  using Raw = typename VecIO<T, VEC>::Raw;
+  const T *values;
+  int64_t d, col;
+  __device__ __forceinline__ Raw raw(int64_t r) const { return VecIO<T, VEC>::load_raw(values + r * d + col); }
+};
+
+// Rows [row0, ...) staged contiguously at `base` (shared memory), row_bytes
+// apart; this thread's vector sits col_bytes into each row.
+template <typename T, int VEC>
+struct SharedRows {
+  using Raw = typename VecIO<T, VEC>::Raw;
+  const char *base;
+  int64_t row0;
+  int row_bytes, col_bytes;
+  __device__ __forceinline__ Raw raw(int64_t r) const {
+    return *reinterpret_cast<const Raw *>(base + static_cast<int>(r - row0) * row_bytes + col_bytes);
+  }
+};
+
+// Fold rows [begin, end) with stride `step` starting at begin + row_lane:
+// batches of kFoldUnroll rows (loads issued together, one recentring test
+// per softmax batch), then the remainder row by row.
+template <typename T, int OP, int VEC, typename Src>
+__device__ __forceinline__ void fold_rows(Acc<OP, VEC> &acc, const Src &src, int64_t begin, int64_t end,
+                                          int64_t row_lane, int64_t step) {
+  constexpr int U = kFoldUnroll;
+  using Raw = typename VecIO<T, VEC>::Raw;
+  int64_t r = begin + row_lane;
+  for (; r + (U - 1) * step < end; r += U * step) {
+    Raw raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
+    float x[U][VEC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) VecIO<T, VEC>::unpack(raw[u], x[u]);
+    acc.template fold_batch<U>(x);
+  }
+  for (; r < end; r += step) {
+    float x[VEC];
+    VecIO<T, VEC>::unpack(src.raw(r), x);
+    acc.fold(x);
+  }
+}
+
+// Per-thread maximum of rows [begin, end) (stride `step` from begin +
+// row_lane), NaN-propagating, -inf when the thread has no rows.  bf16 rows
+// are compared as packed pairs (exact: the maximum of bf16 values is one of
+// them).
+template <typename T, int VEC, typename Src>
+__device__ __forceinline__ void rows_max(float (&m)[VEC], const Src &src, int64_t begin, int64_t end,
+                                         int64_t row_lane, int64_t step) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
+    const __nv_bfloat162 lowest = __floats2bfloat162_rn(-kInf, -kInf);
+    __nv_bfloat162 acc[4] = {lowest, lowest, lowest, lowest};
+    for (int64_t r = begin + row_lane; r < end; r += step) {
+      const uint4 raw = src.raw(r);
+      acc[0] = __hmax2_nan(acc[0], *reinterpret_cast<const __nv_bfloat162 *>(&raw.x));
+      acc[1] = __hmax2_nan(acc[1], *reinterpret_cast<const __nv_bfloat162 *>(&raw.y));
+      acc[2] = __hmax2_nan(acc[2], *reinterpret_cast<const __nv_bfloat162 *>(&raw.z));
+      acc[3] = __hmax2_nan(acc[3], *reinterpret_cast<const __nv_bfloat162 *>(&raw.w));
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t u = *reinterpret_cast<const uint32_t *>(&acc[k]);
+      m[2 * k] = bf16_lo(u);
+      m[2 * k + 1] = bf16_hi(u);
+    }
+  } else {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) m[v] = -kInf;
+    for (int64_t r = begin + row_lane; r < end; r += step) {
+      float x[VEC];
+      VecIO<T, VEC>::unpack(src.raw(r), x);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], x[v]);
+    }
+  }
+}
+
+// Softmax statistics of a thread's rows held in shared memory (read three
+// times in all, HBM once): the exact maximum m, then the mass sum e^(x-m)
+// (terms at most 1, summed plainly).  A thread whose values are all -inf
+// (or that has no rows) contributes no mass; +inf or NaN make the mass NaN
+// through the arithmetic.  The result is an online-statistics accumulator
+// that merges like any other (stats_merge).
+template <typename T, int VEC, typename Src>
+__device__ __forceinline__ void staged_stats(Acc<OP_SOFTMAX, VEC> &acc, const Src &src, int64_t begin, int64_t end,
+                                             int64_t row_lane, int64_t step) {
+  constexpr int U = kFoldUnroll;
+  using Raw = typename VecIO<T, VEC>::Raw;
+  float m[VEC], base[VEC], s[VEC];
+  rows_max<T, VEC>(m, src, begin, end, row_lane, step);
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) {
+    base[v] = m[v] == -kInf ? 0.0f : m[v];  // all -inf: every term is e^-inf = 0
+    s[v] = 0.0f;
+  }
+  if constexpr (VEC % 2 == 0) {
+    constexpr int P = VEC / 2;
+    unsigned long long b2[P], s2[P];
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      b2[k] = pack2(base[2 * k], base[2 * k + 1]);
+      s2[k] = pack2(0.0f, 0.0f);
+    }
+    auto add_row = [&](const Raw &raw) {
+      float x[VEC];
+      VecIO<T, VEC>::unpack(raw, x);
+#pragma unroll
+      for (int k = 0; k < P; ++k) s2[k] = add2_rn(s2[k], exp_diff2(pack2(x[2 * k], x[2 * k + 1]), b2[k]));
+    };
+    int64_t r = begin + row_lane;
+    for (; r + (U - 1) * step < end; r += U * step) {
+      Raw raw[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
+#pragma unroll
+      for (int u = 0; u < U; ++u) add_row(raw[u]);
+    }
+    for (; r < end; r += step) add_row(src.raw(r));
+#pragma unroll
+    for (int k = 0; k < P; ++k) unpack2(s2[k], s[2 * k], s[2 * k + 1]);
+  } else {
+    int64_t r = begin + row_lane;
+    for (; r + (U - 1) * step < end; r += U * step) {
+      Raw raw[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float x[VEC];
+        VecIO<T, VEC>::unpack(raw[u], x);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) s[v] = __fadd_rn(s[v], exp_diff(x[v], base[v]));
+      }
+    }
+    for (; r < end; r += step) {
+      float x[VEC];
+      VecIO<T, VEC>::unpack(src.raw(r), x);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) s[v] = __fadd_rn(s[v], exp_diff(x[v], base[v]));
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) acc.st[v] = Stats{m[v], s[v], 0.0f};
+}
+
+// Merge the row groups of each warp, then the NW warps, leaving the result
+// for column lane cl in part[0][cl] (visible to every thread on return).
+template <int OP, int VEC, int NW>
+__device__ __forceinline__ void cta_merge(Acc<OP, VEC> &acc, Acc<OP, VEC> (*part)[32], int warp, int q, int cl,
+                                          int G) {
+  for (int m = 16; m >= G; m >>= 1) acc.shfl_xor_merge(m);
+  __syncthreads();  // part[] of a previous use has been consumed
+  if (q == 0) part[warp][cl] = acc;
+  __syncthreads();
+  if (warp == 0 && q == 0) {
+    Acc<OP, VEC> total = part[0][cl];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) total.merge(part[w][cl]);
+    part[0][cl] = total;
+  }
+  __syncthreads();
+}
+
+// Merge the row groups of one warp; every lane of column cl gets the total.
+template <int OP, int VEC>
+__device__ __forceinline__ void warp_merge(Acc<OP, VEC> &acc, int G) {
+  for (int m = 16; m >= G; m >>= 1) acc.shfl_xor_merge(m);
+}
+
+// Softmax statistics of a merged accumulator: reference and reciprocal of
+// the total mass per feature.
+template <int VEC>
+__device__ __forceinline__ void stats_of(const Acc<OP_SOFTMAX, VEC> &acc, float (&ref)[VEC], float (&inv)[VEC]) {
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) {
+    ref[v] = acc.st[v].r;
+    inv[v] = stats_inverse(kahan_value(acc.st[v].s, acc.st[v].c));
+  }
+}
+
+// Normalise one row's VEC features: e^(x - ref) * inv, packed in pairs.
+template <int VEC>
+__device__ __forceinline__ void normalize_vec(const float (&x)[VEC], float (&y)[VEC], const float (&ref)[VEC],
+                                              const float (&inv)[VEC]) {
+  if constexpr (VEC % 2 == 0) {
+#pragma unroll
+    for (int k = 0; k < VEC / 2; ++k) {
+      const unsigned long long e =
+          exp_diff2(pack2(x[2 * k], x[2 * k + 1]), pack2(ref[2 * k], ref[2 * k + 1]));
+      unpack2(mul2_rn(e, pack2(inv[2 * k], inv[2 * k + 1])), y[2 * k], y[2 * k + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) y[v] = stats_normalize(x[v], ref[v], inv[v]);
+  }
+}
+
+// Normalise rows [begin, end) (stride `step` from begin + row_lane) with
+// the per-feature reference and reciprocal total; results to out (global).
+template <typename T, int VEC, typename Src>
+__device__ __forceinline__ void normalize_rows(const Src &src, T *__restrict__ out, int64_t d, int64_t col,
+                                               int64_t begin, int64_t end, int64_t row_lane, int64_t step,
+                                               const float (&ref)[VEC], const float (&inv)[VEC]) {
+  constexpr int U = kFoldUnroll;
+  using Raw = typename VecIO<T, VEC>::Raw;
+  int64_t r = begin + row_lane;
+  for (; r + (U - 1) * step < end; r += U * step) {
+    Raw raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float x[VEC], y[VEC];
+      VecIO<T, VEC>::unpack(raw[u], x);
+      normalize_vec<VEC>(x, y, ref, inv);
+      VecIO<T, VEC>::store(out + (r + u * step) * d + col, y);
+    }
+  }
+  for (; r < end; r += step) {
+    float x[VEC], y[VEC];
+    VecIO<T, VEC>::unpack(src.raw(r), x);
+    normalize_vec<VEC>(x, y, ref, inv);
+    VecIO<T, VEC>::store(out + r * d + col, y);
+  }
+}
+
+}  // namespace rgb

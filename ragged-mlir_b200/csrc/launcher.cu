@@ -151,6 +151,7 @@ static int workspace_for(const Problem &p, const Geometry &g, int schedule, int6
   *bytes = 0;
   switch (schedule) {
     case RG_SCHEDULE_NAIVE: return RG_OK;
+    case RG_SCHEDULE_CLASSIFIED: return classified_workspace(p, g, bytes);
     case RG_SCHEDULE_ROWBALANCED: return rowbal_workspace(p, g, bytes);
   }
   return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
@@ -260,6 +261,7 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (schedule) {
     case RG_SCHEDULE_NAIVE: return launch_naive(p, g, s, report);
+    case RG_SCHEDULE_CLASSIFIED: return launch_classified(p, g, workspace, s, report);
     case RG_SCHEDULE_ROWBALANCED: return launch_rowbal(p, g, workspace, s, report);
   }
   return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");

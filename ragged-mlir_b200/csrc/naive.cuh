@@ -84,7 +84,7 @@ naive_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
           ref[v] = fin.st[v].r;
-          total[v] = kahan_value(fin.st[v].s, fin.st[v].c);
+          total[v] = stats_inverse(kahan_value(fin.st[v].s, fin.st[v].c));
         }
         int64_t r = begin + row_lane;
         for (; r + (U - 1) * step < end; r += U * step) {

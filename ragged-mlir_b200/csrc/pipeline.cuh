@@ -1,0 +1,454 @@
+// Pipelined classified worker: one producer warp keeps the next stages of
+// rows in flight with bulk copies while consumer warps reduce the stages
+// already in shared memory.
+//
+// Work is taken in segment order.  The producer claims 32 consecutive
+// segments at a time (one atomic), and packs runs of consecutive short
+// segments (at most `item_rows` rows each) into stages: consecutive
+// segments are contiguous in memory, so a run is ONE bulk copy
+// (cp.async.bulk, TMA's 1-D form) of at most `item_rows` rows.  Segments
+// longer than `item_rows` are the split class: the classify kernel lists
+// them, and after all runs the producer hands out their chunks, each as
+// consecutive stages for one team.  So every row is read from HBM once by the worker; for softmax the
+// statistics and the normalisation both read shared memory.
+//
+// Consumers classify each segment of a run by length, as the reference's
+// classify kernel does (lib/Conversion/ToGPU.cpp:923-998, thresholds of
+// lib/Transforms/Passes.cpp:17-18): a segment of at most 32 rows goes to one
+// warp (shuffles only), a longer one to a team of 4 warps (shuffles, then a
+// named barrier and a fixed-order merge through shared memory).  Split
+// chunks go to a team too; they leave f32 partials, and the team finishing a
+// segment's last chunk merges them (see classified.cuh).
+//
+// Stage protocol: full[s] completes when the producer has written the
+// stage's record and the copy's bytes have landed (arrive.expect_tx +
+// complete_tx); empty[s] completes when every consumer warp is done with the
+// stage.  Every wait is bounded; a wait that gives up records an error in
+// the call's state and the protocol carries on (no thread leaves early, so
+// no named barrier can be left waiting).
+#pragma once
+
+#include "classified.cuh"
+
+namespace rgb {
+
+constexpr int kPipeConsumerWarps = 12;
+constexpr int kPipeTeamWarps = 4;
+constexpr int kPipeTeams = kPipeConsumerWarps / kPipeTeamWarps;
+constexpr int kPipeThreads = 32 * (kPipeConsumerWarps + 1);
+constexpr int kPipeProducer = kPipeConsumerWarps;  // warp index of the producer
+constexpr int kPipeClaim = 32;                     // segments claimed per atomic
+constexpr int kSmemBudget = 227 * 1024;
+
+template <int OP>
+struct PipeStages {
+  static constexpr int value = OP == OP_SOFTMAX ? 4 : 3;
+};
+
+enum : int32_t { STAGE_RUN = 0, STAGE_SPLIT = 1, STAGE_DONE = 2 };
+
+struct StageRecord {
+  int32_t kind;
+  int32_t count;       // RUN: segments in the run
+  int32_t team;        // SPLIT: team that reduces the chunk
+  int32_t pad;
+  int64_t seg;         // RUN: first segment; SPLIT: the split segment
+  int64_t r0, r1;      // rows in the stage
+  int64_t index, first, chunks;  // SPLIT: split-list index, first chunk number, chunk count
+  int64_t chunk;       // SPLIT: chunk number
+  int32_t chunk_first, chunk_last;  // SPLIT: this stage starts / ends its chunk
+  int64_t ends[kPipeClaim];      // RUN: end row of each segment of the run
+};
+
+template <int OP, int VEC>
+struct PipeLayout {
+  static constexpr int kStages = PipeStages<OP>::value;
+  static constexpr int kPartBytes = kPipeConsumerWarps * 32 * static_cast<int>(sizeof(Acc<OP, VEC>));
+  static constexpr int kRecordBytes = kStages * static_cast<int>(sizeof(StageRecord));
+  static constexpr int kBarrierBytes = 2 * kStages * 8 + 64;
+  static constexpr int kStageBytes =
+      ((kSmemBudget - kPartBytes - kRecordBytes - kBarrierBytes - 256) / kStages) / 1024 * 1024;
+  static constexpr int kTotalBytes = kStages * kStageBytes + kPartBytes + kRecordBytes + kBarrierBytes + 128;
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Merge the row groups of a team (kPipeTeamWarps warps), leaving the
+// result for column lane cl in part[tw0 * 32 + cl] where tw0 is the team's
+// first warp; visible to the whole team on return.
+template <int OP, int VEC>
+__device__ __forceinline__ void team_merge(Acc<OP, VEC> &acc, Acc<OP, VEC> *part, int team, int wit, int q, int cl,
+                                           int G) {
+  for (int m = 16; m >= G; m >>= 1) acc.shfl_xor_merge(m);
+  const int base = team * kPipeTeamWarps;
+  named_sync(1 + team, 32 * kPipeTeamWarps);  // part[] of the team's previous merge has been consumed
+  if (q == 0) part[(base + wit) * 32 + cl] = acc;
+  named_sync(1 + team, 32 * kPipeTeamWarps);
+  if (wit == 0 && q == 0) {
+    Acc<OP, VEC> total = part[base * 32 + cl];
+#pragma unroll
+    for (int w = 1; w < kPipeTeamWarps; ++w) total.merge(part[(base + w) * 32 + cl]);
+    part[base * 32 + cl] = total;
+  }
+  named_sync(1 + team, 32 * kPipeTeamWarps);
+}
+
+// Fold rows held in shared memory: softmax takes its exact-maximum
+// statistics (three shared-memory reads), sum and max the plain fold.
+template <typename T, int OP, int VEC, typename Src>
+__device__ __forceinline__ void fold_staged(Acc<OP, VEC> &acc, const Src &src, int64_t begin, int64_t end,
+                                            int64_t row_lane, int64_t step) {
+  if constexpr (OP == OP_SOFTMAX) {
+    staged_stats<T, VEC>(acc, src, begin, end, row_lane, step);
+  } else {
+    fold_rows<T, OP, VEC>(acc, src, begin, end, row_lane, step);
+  }
+}
+
+template <typename T, typename OffT, int OP, int VEC>
+__global__ void __launch_bounds__(kPipeThreads, 1)
+pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out, ClsArgs a) {
+  using L = PipeLayout<OP, VEC>;
+  constexpr int S = L::kStages;
+  constexpr int NC = kPipeConsumerWarps;
+  constexpr int W = PartialWidth<OP>::value;
+  extern __shared__ __align__(128) char smem[];
+  char *const stages = smem;
+  Acc<OP, VEC> *const part = reinterpret_cast<Acc<OP, VEC> *>(smem + S * L::kStageBytes);
+  StageRecord *const rec = reinterpret_cast<StageRecord *>(smem + S * L::kStageBytes + L::kPartBytes);
+  uint64_t *const full = reinterpret_cast<uint64_t *>(smem + S * L::kStageBytes + L::kPartBytes + L::kRecordBytes);
+  uint64_t *const empty = full + S;
+  int *const last_flag = reinterpret_cast<int *>(empty + S);  // [kPipeTeams]
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t d = a.d;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    fence_barrier_init();
+    fence_proxy_async_shared();
+  }
+  __syncthreads();
+
+  const unsigned long long packed = __ldcg(&a.state->split_packed);
+  const int64_t n_split = static_cast<int64_t>(packed & kSplitCountMask);
+  const int64_t n_chunks = static_cast<int64_t>(packed >> kSplitCountBits);
+
+  if (warp == kPipeProducer) {
+    // ------------------------------------------------------------ producer
+    int64_t it = 0;
+    bool ok = true;
+    // Next stage: wait until the consumers released it.
+    auto acquire = [&](int &s) {
+      s = static_cast<int>(it % S);
+      if (it >= S) ok &= mbar_wait(&empty[s], static_cast<uint32_t>(((it / S) - 1) & 1));
+      ++it;
+    };
+    // Publish stage s: record written by this warp, then the copy (if any).
+    auto publish = [&](int s, const void *src, uint32_t bytes) {
+      __syncwarp();
+      if (lane == 0) {
+        if (bytes > 0) {
+          fence_proxy_async_shared();
+          mbar_expect_tx(&full[s], bytes);
+          bulk_copy_g2s(stages + static_cast<int64_t>(s) * L::kStageBytes, src, bytes, &full[s]);
+        } else {
+          mbar_arrive(&full[s]);
+        }
+      }
+    };
+    // Runs of consecutive short segments, 32 segments per claim.  Claims are
+    // prefetched: while the stages of claim k are published, the atomic of
+    // claim k + 2 and the offsets of claim k + 1 are in flight.
+    auto claim_offsets = [&](int64_t base, int64_t &o0, int64_t &o1) {
+      const int64_t sg = base + lane;
+      o0 = sg < a.b ? static_cast<int64_t>(offsets[sg]) : 0;
+      o1 = sg < a.b ? static_cast<int64_t>(offsets[sg + 1]) : 0;
+    };
+    unsigned long long pending = 0;
+    if (lane == 0) pending = atomicAdd(&a.state->work, static_cast<unsigned long long>(kPipeClaim));
+    int64_t base = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
+    if (lane == 0 && base < a.b) pending = atomicAdd(&a.state->work, static_cast<unsigned long long>(kPipeClaim));
+    int64_t o0 = 0, o1 = 0;
+    if (base < a.b) claim_offsets(base, o0, o1);
+    while (base < a.b) {
+      const int64_t next = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
+      if (lane == 0 && next < a.b) pending = atomicAdd(&a.state->work, static_cast<unsigned long long>(kPipeClaim));
+      int64_t n0 = 0, n1 = 0;
+      if (next < a.b) claim_offsets(next, n0, n1);
+      const bool valid = base + lane < a.b;
+      const bool is_long = valid && (o1 - o0) > a.item_rows;
+      const unsigned valid_mask = __ballot_sync(0xffffffffu, valid);
+      const unsigned long_mask = __ballot_sync(0xffffffffu, is_long);
+      int i = 0;
+      while (i < 32 && ((valid_mask >> i) & 1u)) {
+        if ((long_mask >> i) & 1u) {
+          ++i;
+          continue;
+        }
+        // Extend the run from segment i while segments are short and the
+        // rows fit one stage.
+        const int64_t start = __shfl_sync(0xffffffffu, o0, i);
+        const bool stop = lane >= i && (!valid || is_long || o1 - start > a.item_rows);
+        const unsigned stop_mask = __ballot_sync(0xffffffffu, stop) & (~0u << i);
+        const int j = stop_mask ? __ffs(stop_mask) - 1 : 32;  // first segment not in the run
+        const int64_t end = __shfl_sync(0xffffffffu, o1, j - 1);
+        int s;
+        acquire(s);
+        StageRecord &r = rec[s];
+        if (lane == 0) {
+          r.kind = STAGE_RUN;
+          r.count = j - i;
+          r.seg = base + i;
+          r.r0 = start;
+          r.r1 = end;
+        }
+        if (lane >= i && lane < j) r.ends[lane - i] = o1;
+        publish(s, values + start * d, static_cast<uint32_t>((end - start) * a.row_bytes));
+        i = j;
+      }
+      base = next;
+      o0 = n0;
+      o1 = n1;
+    }
+    // Split chunks in chunk order, kSplitClaim per atomic (the next claim in
+    // flight); each chunk is published as consecutive stages for one team.
+    // Lane l caches split entry wbase + l (first chunk, segment, rows), so
+    // walking consecutive chunks needs no search.
+    constexpr int kSplitClaim = 4;
+    int team = 0;
+    int64_t wbase = -1, w_first = INT64_MAX, w_seg = 0, w_begin = 0, w_end = 0, w_rows = 1, w_chunks = 0;
+    auto load_window = [&](int64_t start) {
+      wbase = start;
+      const int64_t idx = start + lane;
+      const bool v = idx < n_split;
+      w_first = v ? __ldcg(a.split_base + idx) : INT64_MAX;
+      w_seg = v ? __ldcg(a.split_seg + idx) : 0;
+      w_begin = v ? static_cast<int64_t>(offsets[w_seg]) : 0;
+      w_end = v ? static_cast<int64_t>(offsets[w_seg + 1]) : 0;
+      w_rows = v ? chunk_rows_of(w_end - w_begin, a.item_rows) : 1;
+      w_chunks = v ? (w_end - w_begin + w_rows - 1) / w_rows : 0;
+    };
+    // Lane whose entry holds chunk c, or -1.
+    auto find = [&](int64_t c) -> int {
+      const unsigned m = __ballot_sync(0xffffffffu, w_first <= c && c < w_first + w_chunks);
+      return m ? __ffs(m) - 1 : -1;
+    };
+    if (lane == 0) pending = atomicAdd(&a.state->split_work, static_cast<unsigned long long>(kSplitClaim));
+    for (;;) {
+      const int64_t c0 = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
+      if (c0 >= n_chunks) break;
+      if (lane == 0) pending = atomicAdd(&a.state->split_work, static_cast<unsigned long long>(kSplitClaim));
+      const int64_t c1 = c0 + kSplitClaim < n_chunks ? c0 + kSplitClaim : n_chunks;
+      for (int64_t c = c0; c < c1; ++c) {
+        int k = find(c);
+        if (k < 0) {
+          // 32-ary search of the split list for the last i with base[i] <= c.
+          int64_t lo = 0, hi = n_split - 1;
+          while (lo < hi) {
+            const int64_t step = (hi - lo + 31) / 32;
+            const int64_t probe = lo + (lane + 1) * step;
+            const bool le = probe <= hi && __ldcg(a.split_base + probe) <= c;
+            const unsigned m = __ballot_sync(0xffffffffu, le);
+            const int n = m ? 32 - __clz(m) : 0;  // probes lo + 1..n*step are <= c
+            const int64_t cut = lo + static_cast<int64_t>(n + 1) * step - 1;
+            hi = n < 32 && cut < hi ? cut : hi;
+            lo = lo + static_cast<int64_t>(n) * step;
+          }
+          load_window(lo);
+          k = find(c);
+        }
+        const int64_t seg = __shfl_sync(0xffffffffu, w_seg, k);
+        const int64_t first = __shfl_sync(0xffffffffu, w_first, k);
+        const int64_t begin = __shfl_sync(0xffffffffu, w_begin, k);
+        const int64_t end = __shfl_sync(0xffffffffu, w_end, k);
+        const int64_t rows_per_chunk = __shfl_sync(0xffffffffu, w_rows, k);
+        const int64_t chunks = __shfl_sync(0xffffffffu, w_chunks, k);
+        const int64_t r0 = begin + (c - first) * rows_per_chunk;
+        const int64_t r1 = r0 + rows_per_chunk < end ? r0 + rows_per_chunk : end;
+        for (int64_t a0 = r0; a0 < r1; a0 += a.item_rows) {
+          const int64_t a1 = a0 + a.item_rows < r1 ? a0 + a.item_rows : r1;
+          int s;
+          acquire(s);
+          if (lane == 0) {
+            StageRecord &r = rec[s];
+            r.kind = STAGE_SPLIT;
+            r.team = team;
+            r.seg = seg;
+            r.r0 = a0;
+            r.r1 = a1;
+            r.index = wbase + k;
+            r.first = first;
+            r.chunks = chunks;
+            r.chunk = c;
+            r.chunk_first = a0 == r0;
+            r.chunk_last = a1 == r1;
+          }
+          publish(s, values + a0 * d, static_cast<uint32_t>((a1 - a0) * a.row_bytes));
+        }
+        team = team + 1 == kPipeTeams ? 0 : team + 1;
+      }
+    }
+    int s;
+    acquire(s);
+    if (lane == 0) rec[s].kind = STAGE_DONE;
+    publish(s, nullptr, 0);
+    if (!ok && lane == 0) atomicExch(&a.state->error, 1ull);
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int G = 1 << a.g_shift;
+  const int q = lane >> a.g_shift, cl = lane & (G - 1);
+  const bool active = cl < a.vec_cols;
+  const int64_t col = static_cast<int64_t>(cl) * VEC;
+  const int col_bytes = cl * VEC * static_cast<int>(sizeof(T));
+  const int team = warp / kPipeTeamWarps, wit = warp % kPipeTeamWarps;
+  const int64_t warp_step = 32 >> a.g_shift;
+  const int64_t team_step = static_cast<int64_t>(kPipeTeamWarps) << (5 - a.g_shift);
+  const int64_t team_lane = static_cast<int64_t>(wit) * (32 >> a.g_shift) + q;
+  bool ok = true;
+  Acc<OP, VEC> split_acc;  // this team's chunk in progress (stages of one chunk arrive in order)
+  split_acc.init();
+  // Round-robin owners of warp-class segments (warps) and CTA-class segments
+  // (teams), counted over the whole stage sequence, which every consumer
+  // warp walks identically.
+  int small_i = 0, medium_i = 0;
+  for (int64_t it = 0;; ++it) {
+    const int s = static_cast<int>(it % S);
+    ok &= mbar_wait(&full[s], static_cast<uint32_t>((it / S) & 1));
+    const StageRecord &r = rec[s];
+    const int kind = r.kind;
+    if (kind == STAGE_DONE) break;
+    const SharedRows<T, VEC> rows{stages + static_cast<int64_t>(s) * L::kStageBytes, r.r0, a.row_bytes, col_bytes};
+    if (kind == STAGE_RUN) {
+      int64_t begin = r.r0;
+      const int count = r.count;
+      for (int k = 0; k < count; ++k) {
+        const int64_t end = r.ends[k];
+        const int64_t seg = r.seg + k;
+        if (end - begin <= kWarpClassMax) {
+          // ---- warp class: one warp
+          const bool mine = small_i == warp;
+          small_i = small_i + 1 == NC ? 0 : small_i + 1;
+          if (mine) {
+            Acc<OP, VEC> acc;
+            acc.init();
+            if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, q, warp_step);
+            warp_merge<OP, VEC>(acc, G);
+            if constexpr (OP == OP_SOFTMAX) {
+              if (active) {
+                float ref[VEC], inv[VEC];
+                stats_of<VEC>(acc, ref, inv);
+                normalize_rows<T, VEC>(rows, out, d, col, begin, end, q, warp_step, ref, inv);
+              }
+            } else if (q == 0 && active) {
+              float y[VEC];
+              acc.result(y);
+              VecIO<T, VEC>::store(out + seg * d + col, y);
+            }
+          }
+        } else {
+          const bool ours = medium_i == team;
+          medium_i = medium_i + 1 == kPipeTeams ? 0 : medium_i + 1;
+          if (!ours) {
+            begin = end;
+            continue;
+          }
+          // ---- CTA class: one team
+          Acc<OP, VEC> acc;
+          acc.init();
+          if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, team_lane, team_step);
+          team_merge<OP, VEC>(acc, part, team, wit, q, cl, G);
+          const Acc<OP, VEC> &fin = part[(team * kPipeTeamWarps) * 32 + cl];
+          if constexpr (OP == OP_SOFTMAX) {
+            if (active) {
+              float ref[VEC], inv[VEC];
+              stats_of<VEC>(fin, ref, inv);
+              normalize_rows<T, VEC>(rows, out, d, col, begin, end, team_lane, team_step, ref, inv);
+            }
+          } else if (wit == 0 && q == 0 && active) {
+            float y[VEC];
+            fin.result(y);
+            VecIO<T, VEC>::store(out + seg * d + col, y);
+          }
+        }
+        begin = end;
+      }
+    } else if (r.team == team) {
+      // ---- split chunk: one team folds the chunk's stages, publishes an
+      // f32 partial, and the team finishing the segment's last chunk merges
+      const int64_t c = r.chunk, index = r.index, first = r.first, chunks = r.chunks, seg = r.seg;
+      if (r.chunk_first) split_acc.init();
+      if (active) {
+        if constexpr (OP == OP_SOFTMAX) {
+          Acc<OP, VEC> stage_acc;
+          staged_stats<T, VEC>(stage_acc, rows, r.r0, r.r1, team_lane, team_step);
+          split_acc.merge(stage_acc);
+        } else {
+          fold_rows<T, OP, VEC>(split_acc, rows, r.r0, r.r1, team_lane, team_step);
+        }
+      }
+      if (!r.chunk_last) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        continue;
+      }
+      Acc<OP, VEC> acc = split_acc;
+      team_merge<OP, VEC>(acc, part, team, wit, q, cl, G);
+      Acc<OP, VEC> *const fin = &part[(team * kPipeTeamWarps) * 32];
+      if (wit == 0 && q == 0 && active) store_partial<OP, VEC>(fin[cl], a.partials + (c * W) * d + col, d);
+      __threadfence();  // release: the partial before the count
+      named_sync(1 + team, 32 * kPipeTeamWarps);
+      if (wit == 0 && lane == 0) last_flag[team] = atomicAdd(a.done + index, 1u) == static_cast<unsigned>(chunks - 1);
+      named_sync(1 + team, 32 * kPipeTeamWarps);
+      if (last_flag[team]) {
+        __threadfence();  // acquire: every chunk's partial is visible
+        Acc<OP, VEC> m;
+        m.init();
+        if (active) {
+          int64_t j = first + team_lane;
+          for (; j + 3 * team_step < first + chunks; j += 4 * team_step) {
+            Acc<OP, VEC> p0, p1, p2, p3;  // four loads in flight
+            load_partial<OP, VEC>(p0, a.partials + (j * W) * d + col, d);
+            load_partial<OP, VEC>(p1, a.partials + ((j + team_step) * W) * d + col, d);
+            load_partial<OP, VEC>(p2, a.partials + ((j + 2 * team_step) * W) * d + col, d);
+            load_partial<OP, VEC>(p3, a.partials + ((j + 3 * team_step) * W) * d + col, d);
+            p0.merge(p1);
+            p2.merge(p3);
+            p0.merge(p2);
+            m.merge(p0);
+          }
+          for (; j < first + chunks; j += team_step) {
+            Acc<OP, VEC> pj;
+            load_partial<OP, VEC>(pj, a.partials + (j * W) * d + col, d);
+            m.merge(pj);
+          }
+        }
+        team_merge<OP, VEC>(m, part, team, wit, q, cl, G);
+        if (wit == 0 && q == 0 && active) {
+          if constexpr (OP == OP_SOFTMAX) {
+            store_partial<OP, VEC>(fin[cl], a.seg_stats + index * 2 * d + col, d);
+          } else {
+            float y[VEC];
+            fin[cl].result(y);
+            VecIO<T, VEC>::store(out + seg * d + col, y);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (!ok && lane == 0) atomicExch(&a.state->error, 1ull);
+}
+
+}  // namespace rgb

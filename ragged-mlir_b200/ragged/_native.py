@@ -37,7 +37,8 @@ class Report(ctypes.Structure):
                 ("kernel_ids", ctypes.c_int32 * MAX_LAUNCHES), ("grid", (ctypes.c_int32 * 3) * MAX_LAUNCHES),
                 ("block", ctypes.c_int32 * MAX_LAUNCHES), ("shared_bytes", ctypes.c_int32 * MAX_LAUNCHES),
                 ("memsets", ctypes.c_int32), ("d_vector", ctypes.c_int32), ("d_tile", ctypes.c_int32),
-                ("streams", ctypes.c_int32), ("workspace_bytes", ctypes.c_int64)]
+                ("streams", ctypes.c_int32), ("workspace_bytes", ctypes.c_int64),
+                ("thresholds", ctypes.c_int64 * 2)]
 
 
 class DeviceInfo(ctypes.Structure):

@@ -28,6 +28,8 @@ from .selection import default_model
 I64_MAX = 2**63 - 1
 # Segment-length class bounds of the classified schedule (warp <= 32 rows,
 # CTA <= 4096 rows, longer ones split), as in the reference's Passes.cpp:17-18.
+# A call reports the bounds it used: the CTA bound shrinks to 64 KiB of one
+# column tile for wide rows.
 THRESHOLDS = (32, 4096)
 
 _lock = threading.RLock()
@@ -226,6 +228,7 @@ class CompiledProgram:
         return self._report(schedule, selection, started, report, nbytes)
 
     def _report(self, schedule, selection, started, report, nbytes) -> ExecutionReport:
+        thresholds = THRESHOLDS if schedule == "classified" else ()
         if report is None:
             names, grids, vec, tile, streams = (), (), 1, None, 1
         else:
@@ -233,9 +236,11 @@ class CompiledProgram:
             names = tuple(_native.kernel_name(report.kernel_ids[i]) for i in range(count))
             grids = tuple(tuple(int(x) for x in report.grid[i]) for i in range(count))
             vec, tile, streams = int(report.d_vector), int(report.d_tile), int(report.streams)
+            if schedule == "classified" and report.thresholds[1] > 0:
+                thresholds = (int(report.thresholds[0]), int(report.thresholds[1]))
         classes = ("cta",) if schedule == "naive" else (("warp", "cta", "split") if schedule == "classified"
                                                         else ("rows",))
-        return ExecutionReport(classes, THRESHOLDS if schedule == "classified" else (), grids, nbytes, self._digest,
+        return ExecutionReport(classes, thresholds, grids, nbytes, self._digest,
                                None, "validated", names, (time.perf_counter() - started) * 1000,
                                cache_hit=self.cache_hit, optimizations={"requested": self.spec.optimizations.to_dict()},
                                d_tile=tile, d_vector=vec, streams=streams, selected=schedule, selection=selection)

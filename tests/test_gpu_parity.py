@@ -241,3 +241,50 @@ def test_narrow_rows_packed_and_unaligned(cuda, op, dtype, d):
             assert "rowbalanced_packed" in names
         else:
             assert "rowbalanced" in names and "rowbalanced_packed" not in names
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+@pytest.mark.parametrize("dtype,d", [("f32", 3), ("bf16", 128), ("f32", 1024)])
+def test_classified_many_split_segments(cuda, op, dtype, d):
+    """Dozens of split-class segments (several chunks each, one ending on a
+    chunk boundary) between warp- and CTA-class ones and empty segments:
+    the split list, chunk numbering and last-chunk merge of the classified
+    schedule, across column tiles for D=1024."""
+    rng = np.random.default_rng(31)
+    count = 24 if d <= 128 else 6
+    lengths = []
+    for i in range(count):
+        lengths += [int(rng.integers(4097, 20000)), 0, int(rng.integers(1, 33)), int(rng.integers(33, 4097))]
+    lengths[4] = 3 * 4096  # exactly three chunks
+    offsets = offsets_of(np.array(lengths, dtype=np.int64))
+    values = prepared(rng.normal(size=(int(offsets[-1]), d)), dtype)
+    _run_all(cuda, op, dtype, values, offsets)
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+def test_classified_is_deterministic(cuda, op):
+    """Work items go to CTAs through an atomic counter; the output must not
+    depend on which CTA took which item."""
+    lengths = make_lengths("long_tail", 3000, 400_000, seed=41)
+    offsets = offsets_of(lengths)
+    values = np.random.default_rng(42).normal(size=(int(offsets[-1]), 32)).astype(np.float32)
+    first, report = run_device(cuda, op, "f32", values, offsets, select="classified")
+    assert report.kernel_names[:2] == ("classify", "classified_worker")
+    for _ in range(3):
+        again, _ = run_device(cuda, op, "f32", values, offsets, select="classified")
+        np.testing.assert_array_equal(again, first)
+    check(first, values, offsets, op, "f32")
+
+
+@pytest.mark.parametrize("op,rows", [("sum", 200_000), ("max", 200_000), ("softmax", 150_000)])
+def test_classified_chunks_grow_for_giant_segments(cuda, op, rows):
+    """A split segment longer than 1024 chunks of one stage gets longer
+    chunks (each streamed through several shared-memory stages by one team);
+    its last chunk merges at most 1024 partials."""
+    lengths = np.array([5, rows, 0, 7], dtype=np.int64)
+    offsets = offsets_of(lengths)
+    values = prepared(np.random.default_rng(53).normal(size=(int(offsets[-1]), 256)), "bf16")
+    actual, report = run_device(cuda, op, "bf16", values, offsets, select="classified")
+    assert report.thresholds[0] == 32 and 32 < report.thresholds[1] <= 4096
+    assert rows > 1024 * report.thresholds[1]
+    check(actual, values, offsets, op, "bf16")
