@@ -241,8 +241,10 @@ def config_dict(w, args, flush) -> dict:
 
 # ---------------------------------------------------------------- ours ----
 
-def time_calls(torch, fn, steps, warmup, stream, flush=None):
-    """Per-step device time (ms) with CUDA events on ``stream``."""
+def time_calls(torch, fn, steps, warmup, stream, flush=None, dist=None):
+    """Per-step device time (ms) with CUDA events on ``stream``; with
+    ``dist`` every step is bracketed by a barrier and a synchronize, and the
+    per-step time is the maximum over ranks."""
     for _ in range(warmup):
         if flush is not None:
             flush()
@@ -253,30 +255,46 @@ def time_calls(torch, fn, steps, warmup, stream, flush=None):
     for i in range(steps):
         if flush is not None:
             flush()
+        if dist is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
         starts[i].record(stream)
         fn()
         ends[i].record(stream)
+        if dist is not None:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
-    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if dist is not None:
+        t = torch.tensor(times, dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times = t.cpu().tolist()
+    return times
 
 
 def ours(args) -> None:
     import torch
     from ragged import ArtifactCache, Compiler, ProgramSpec
-    from ragged import _native
+    from ragged.sharding import segment_owners, shard_rows, torch_exchange
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    if world > 1:
-        raise SystemExit("multi-GPU runs need the sharded path (not built yet)")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     w = workloads.make(args.workload, scale=args.scale)
+    if world > 1 and w.op == "softmax":
+        raise SystemExit("sharded calls compute sum and max; run softmax workloads with --gpus 1")
     offsets_host = w.offsets()
-    values = device_values(torch, w, (0, w.n), device)
+    rows = shard_rows(w.n, world, rank)
+    values = device_values(torch, w, rows, device)
     offsets = torch.from_numpy(offsets_host).to(device)
     tdtype = values.dtype
     rows_out = w.n if w.op == "softmax" else w.b
@@ -296,37 +314,62 @@ def ours(args) -> None:
         flush_note = "L2 flushed between steps (2x L2 buffer rewritten)"
 
     report_holder = {}
+    exchange = torch_exchange() if world > 1 else None
 
     def step():
-        report_holder["r"] = program.run(values, offsets, out, select=select, max_len=max_len)
+        if world > 1:
+            report_holder["r"] = program.run_sharded(values, offsets, out, total_rows=w.n, world=world, rank=rank,
+                                                     exchange=exchange)
+        else:
+            report_holder["r"] = program.run(values, offsets, out, select=select, max_len=max_len)
 
     flush = (lambda: flush_l2(torch, flush_buffer)) if flush_buffer is not None else None
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        times = time_calls(torch, step, args.steps, args.warmup, stream, flush)
+        times = time_calls(torch, step, args.steps, args.warmup, stream, flush, dist)
     report = report_holder["r"]
     ms = statistics.mean(times)
     nbytes = w.algorithmic_bytes()
     value = nbytes / (ms / 1e3) / 1e9
     peak, peak_kind = peak_hbm()
-    launches = len(report.kernel_names) * args.steps
+    per_rank = nbytes / world
+    launches = (len(report.kernel_names) + (1 if world > 1 else 0)) * args.steps
     line = {"metric": metric_name(), "value": round(value, 2), "unit": "GB/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_dict(w, args, flush_note), "schedule_selected": report.selected,
-            "kernels": list(report.kernel_names), "gpu_launches": launches,
+            "kernels": list(report.kernel_names) + (["shard_combine"] if world > 1 else []),
+            "gpu_launches": launches,
             "step_times_ms": [round(t, 4) for t in times],
-            "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(value / peak, 4), "traffic": None,
+            "roofline": {"bound": "hbm", "achieved": round(per_rank / (ms / 1e3) / 1e9, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(per_rank / (ms / 1e3) / 1e9 / peak, 4), "traffic": None,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback 6650 GB/s", "kernel": "whole call (all kernels of the schedule)"},
+                         else "fallback 6650 GB/s",
+                         "kernel": "whole call per GPU (all kernels of the schedule; the slowest rank)"},
             "clocks": clocks.summary()}
+    if world > 1:
+        line["sharding"] = {"rows_per_rank": [list(shard_rows(w.n, world, r)) for r in range(world)],
+                            "collective": "NCCL all-gather of edge records",
+                            "edge_bytes_per_rank": _native_edge_bytes(w)}
     if not args.no_e2e:
-        line["e2e"] = e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream)
-    if not args.no_cpu_baseline and rank == 0:
+        owners = segment_owners(offsets_host, world) if w.op != "softmax" else None
+        line["e2e"] = e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream, dist,
+                              rows, owners, rank, world, exchange)
+    if not args.no_cpu_baseline and rank == 0 and world == 1:
         line["cpu_baseline"] = {k: v for k, v in run_cpu_baseline(w, args.cpu_seconds).items()
                                 if k != "seconds_per_call"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _native_edge_bytes(w) -> int:
+    from ragged import _native
+    return _native.shard_edge_bytes(w.op, w.d)
 
 
 def host_memory_available() -> int:
@@ -339,33 +382,50 @@ def host_memory_available() -> int:
     return 0
 
 
-def e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream) -> dict:
-    """Same metric with inputs in pinned host memory; copies inside the timed region."""
-    world = int(os.environ.get("WORLD_SIZE", "1"))
+def e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream, dist=None, rows=None,
+            owners=None, rank=0, world=1, exchange=None) -> dict:
+    """Same metric with inputs in pinned host memory; every step copies this
+    rank's rows and the offsets in and the rows of out this rank finishes
+    back, inside the timed region (max over ranks)."""
     need = values.numel() * values.element_size() + out.numel() * out.element_size() + offsets_host.nbytes
     available = host_memory_available()
-    if need * world > 0.6 * available:
+    skip = need * world > 0.6 * available
+    if dist is not None:
+        flag = torch.tensor([1 if skip else 0], device=values.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        skip = bool(flag.item())
+    if skip:
         return {"value": None, "unit": "GB/s", "h2d_bytes_per_step": need, "d2h_bytes_per_step": None,
                 "skipped": f"pinned host buffers ({need * world / 1e9:.1f} GB over all ranks) exceed 60% of "
                            f"MemAvailable ({available / 1e9:.1f} GB)"}
     host_values = torch.empty(values.shape, dtype=values.dtype, pin_memory=True)
     host_values.copy_(values)
     host_offsets = torch.from_numpy(offsets_host).pin_memory()
-    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    if owners is not None:
+        mine = np.nonzero(owners == rank)[0]
+        first, last = (int(mine[0]), int(mine[-1]) + 1) if mine.size else (0, 0)
+    else:
+        first, last = 0, out.shape[0]
+    host_out = torch.empty((last - first, out.shape[1]), dtype=out.dtype, pin_memory=True)
     dev_offsets = torch.empty_like(host_offsets, device=values.device)
 
     def step():
         values.copy_(host_values, non_blocking=True)
         dev_offsets.copy_(host_offsets, non_blocking=True)
-        program.run(values, dev_offsets, out, select=select, max_len=max_len)
-        host_out.copy_(out, non_blocking=True)
+        if world > 1:
+            program.run_sharded(values, dev_offsets, out, total_rows=w.n, world=world, rank=rank, exchange=exchange)
+        else:
+            program.run(values, dev_offsets, out, select=select, max_len=max_len)
+        host_out.copy_(out[first:last], non_blocking=True)
 
-    times = time_calls(torch, step, args.steps, 1, stream)
+    times = time_calls(torch, step, args.steps, 1, stream, None, dist)
     ms = statistics.mean(times)
     h2d = host_values.numel() * host_values.element_size() + host_offsets.numel() * host_offsets.element_size()
     d2h = host_out.numel() * host_out.element_size()
     return {"value": round(w.algorithmic_bytes() / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
-            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ms, 3)}
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ms, 3),
+            "note": "per rank: its rows and the offsets in, the output rows it finishes out" if world > 1 else
+                    "values and offsets in, all output rows out"}
 
 
 def main() -> None:

@@ -125,6 +125,45 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
 /* Name of a kernel id reported in rg_report.kernel_ids ("" if unknown). */
 const char *rg_kernel_name(int kernel_id);
 
+/* ------------------------------------------------ sharded calls (multi-GPU)
+ *
+ * One process per GPU.  Rank r of `world` holds rows [row0, row1) of the
+ * packed values (rg_shard_rows: a row-balanced split) and the whole offsets
+ * array.  rg_run_shard reduces the rank's rows and writes every segment
+ * that ends in its rows and started there; the pieces of the segments cut
+ * at its edges go to its edge record.  The caller all-gathers the edge
+ * records of all ranks in rank order (e.g. NCCL all-gather; a few KB per
+ * rank) and calls rg_shard_combine, which writes the cut segments this rank
+ * finishes.  Together the ranks write every output row exactly once (each
+ * on the rank that holds the segment's end).  Sum and max only.
+ * The reference is single-GPU; these entry points are this build's
+ * multi-GPU extension of its launcher (runtime/Driver.h:21-54). */
+
+/* Rows [*row0, *row1) of rank `rank` in a row-balanced split of n rows. */
+int rg_shard_rows(int64_t n, int world, int rank, int64_t *row0, int64_t *row1);
+
+/* Bytes of one rank's edge record (header + two f32 pieces of D features). */
+int rg_shard_edge_bytes(int op, int64_t d, int64_t *bytes);
+
+/* Scratch bytes rg_run_shard needs (256-byte aligned) on the current device. */
+int rg_shard_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world,
+                             int rank, uint32_t flags, int64_t *bytes);
+
+/* Reduce rank `rank`'s rows (rg_shard_rows) of a call over n rows and b
+ * segments: values holds those rows (the first first), offsets all b + 1
+ * entries, out all b rows (only the rows this rank finishes are written),
+ * edges this rank's edge record (rg_shard_edge_bytes, 16-byte aligned
+ * device memory).  Segments that end at row 0 belong to rank 0. */
+int rg_run_shard(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world, int rank,
+                 const void *values, const void *offsets, void *out, void *edges, void *workspace,
+                 int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report);
+
+/* Finish the segments cut by shard boundaries that this rank owns, from
+ * the gathered edge records of ranks 0..world-1 (device memory, rank
+ * order). */
+int rg_shard_combine(int op, int dtype, int64_t d, int world, int rank, const void *gathered, void *out,
+                     uint32_t flags, void *stream);
+
 /* Row-balanced segmented sum or max that allocates nothing and takes no
  * workspace: for callers that may not allocate device memory (a host that
  * reserves all device memory for its own pool, a plugin callback that may

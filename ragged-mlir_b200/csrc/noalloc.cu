@@ -95,12 +95,12 @@ int run_typed(const Problem &p, const Geometry &g, const DeviceProps &dev, void 
   dim3 grid(static_cast<unsigned>(ctas), g.col_tiles, 1);
   rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
-      p.d, g.g_shift, g.vec_cols, units, pieces, meta);
+      p.d, g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{0, p.n, 1});
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch (no-alloc)");
   if (status || ctas < 2) return status;
   dim3 fix_grid(static_cast<unsigned>(ctas), g.col_tiles, 1);
   rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d,
-                                                                          g.vec_cols, ctas, pieces, meta);
+                                                                          g.vec_cols, ctas, pieces, meta, nullptr);
   return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch (no-alloc)");
 }
 

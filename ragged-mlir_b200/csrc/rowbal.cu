@@ -114,7 +114,7 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
       if (status || plan.ctas < 2) return status;
       dim3 fix_grid(static_cast<unsigned>(plan.ctas), 1, 1);
       rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d,
-                                                                              g.vec_cols, plan.ctas, pieces, meta);
+                                                                              g.vec_cols, plan.ctas, pieces, meta, nullptr);
       record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
       return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
     }
@@ -135,13 +135,13 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   dim3 grid(plan.ctas, g.col_tiles, 1);
   rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
-      p.d, g.g_shift, g.vec_cols, plan.units, pieces, meta);
+      p.d, g.g_shift, g.vec_cols, plan.units, pieces, meta, RowWindow{0, p.n, 1});
   record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch");
   if (status || plan.ctas < 2) return status;
   dim3 fix_grid(static_cast<unsigned>(plan.ctas), g.col_tiles, 1);
   rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols,
-                                                                          plan.ctas, pieces, meta);
+                                                                          plan.ctas, pieces, meta, nullptr);
   record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
   return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
 }

@@ -234,12 +234,59 @@ __device__ __forceinline__ void combine_pieces(int count, PieceFn piece, int pst
   }
 }
 
+// Rows of the whole array that one launch covers.  A single-GPU call covers
+// [0, N); a rank of a sharded call covers its own rows [row0, row1), with
+// values[0] holding row row0 (see shard.cu).
+struct RowWindow {
+  int64_t row0, row1;
+  int first;  // the first window: it also consumes the segment ends at row 0
+};
+
+// Segment ends at or before row `row`: the first k in [0, B] with
+// offsets[k+1] > row (G-ary search by the G lanes of a group; every lane
+// returns the same answer).
+template <typename OffT>
+__device__ int64_t ends_upto(const OffT *offsets, int64_t b, int64_t row, int g, int gl, unsigned group_mask,
+                             int group_base) {
+  int64_t lo = 0, hi = b;
+  while (hi - lo > 0) {
+    const int64_t span = hi - lo;
+    const int64_t step = (span + g) / (g + 1) > 0 ? (span + g) / (g + 1) : 1;
+    const int64_t k = lo + static_cast<int64_t>(gl + 1) * step - 1;
+    const bool valid = k < hi;
+    const bool pred = valid && load_offset(offsets, k + 1) > row;
+    const unsigned ballot = __ballot_sync(group_mask, pred) >> group_base;
+    const unsigned valid_bits = __ballot_sync(group_mask, valid) >> group_base;
+    if (ballot) {
+      const int first = __ffs(ballot) - 1;
+      hi = lo + static_cast<int64_t>(first + 1) * step - 1;
+      lo = lo + static_cast<int64_t>(first) * step;
+    } else {
+      const int last = 31 - __clz(valid_bits);
+      lo = lo + static_cast<int64_t>(last + 1) * step;
+    }
+    if (lo > hi) lo = hi;
+  }
+  return lo;
+}
+
+// Merge-path diagonal after row `row` - 1 and every segment end at or
+// before `row`: where a window starting or ending at `row` is cut.  The
+// first window starts at diagonal 0 instead (it also consumes the ends at
+// row 0: empty segments at the start, or every segment when N = 0).
+template <typename OffT>
+__device__ __forceinline__ int64_t window_diag(const OffT *offsets, int64_t n, int64_t b, int64_t row, int g,
+                                               int gl, unsigned group_mask, int group_base) {
+  if (row >= n) return n + b;
+  return row + ends_upto(offsets, b, row, g, gl, group_mask, group_base);
+}
+
 template <typename T, typename OffT, int OP, int VEC, int U = RowbalTuning::kUnroll,
           bool DB = RowbalTuning::kDoubleBuffer, int MINB = RowbalTuning::kMinBlocks>
 __global__ void __launch_bounds__(kRowbalThreads, MINB)
 rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
               int64_t n, int64_t b, int64_t d, int g_shift, int vec_cols, int64_t units,
-              float *__restrict__ pieces, UnitMeta *__restrict__ meta) {
+              float *__restrict__ pieces, UnitMeta *__restrict__ meta, RowWindow window) {
   using Acc = RowAcc<OP, VEC>;
   const int lane = threadIdx.x & 31;
   const int G = 1 << g_shift;
@@ -255,8 +302,10 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   const int64_t col = static_cast<int64_t>(cv) * VEC;
 
   // This unit's slice of the merge path.
-  const int64_t path = n + b;
-  const int64_t d0 = path / units * unit + min(unit, path % units);
+  const int64_t d_lo = window.first ? 0 : window_diag(offsets, n, b, window.row0, G, gl, group_mask, group_base);
+  const int64_t d_hi = window_diag(offsets, n, b, window.row1, G, gl, group_mask, group_base);
+  const int64_t path = d_hi - d_lo;
+  const int64_t d0 = d_lo + path / units * unit + min(unit, path % units);
   const int64_t d1 = d0 + path / units + (unit < path % units ? 1 : 0);
   const int64_t i0 = path_search(offsets, b, d0, G, gl, group_mask, group_base);
   const int64_t i1 = path_search(offsets, b, d1, G, gl, group_mask, group_base);
@@ -314,7 +363,7 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   // one is folded, so a warp always has loads pending.  A batch without a
   // segment boundary takes the fast path (no per-row boundary test).
   using Raw = typename VecIO<T, VEC>::Raw;
-  const T *ptr = values + j0 * d + col;
+  const T *ptr = values + (j0 - window.row0) * d + col;
   auto load_batch = [&](Raw (&raw)[U], int64_t rel) {  // rows j0 + rel .. + U
 #pragma unroll
     for (int t = 0; t < U; ++t)
@@ -540,69 +589,174 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
 // CTA where the segment starts (its TAIL piece).  The fix-up CTA first
 // finds the chain's end -- the CTA holding the HEAD piece -- scanning
 // kFixupThreads metadata entries per step, then its warps merge contiguous
-// runs of the THROUGH pieces between in parallel, and warp 0 merges TAIL,
-// the warps' partials (in order) and HEAD.  The merge tree depends only on
-// the chain, so results are deterministic.
+// runs of the pieces in between in parallel, and warp 0 merges the runs'
+// partials in order and the HEAD.  The merge tree depends only on the
+// chain, so results are deterministic.
+//
+// Sharded calls (edges != nullptr) have open chains at the window's edges:
+// the segment open at the window's start (started on an earlier rank: THROUGH
+// pieces up to its HEAD, or through the whole window) and the one open at
+// its end (TAIL and THROUGH pieces, no HEAD).  Their merged f32 pieces go
+// to the window's edge record instead of out; one extra CTA (blockIdx.x ==
+// units) handles the start and writes the record's header.
 constexpr int kFixupThreads = 256;
 
-template <typename T, int OP, int VEC>
-__global__ void __launch_bounds__(kFixupThreads)
-rowbal_fixup_kernel(T *__restrict__ out, int64_t d, int vec_cols, int64_t units,
-                    const float *__restrict__ pieces, const UnitMeta *__restrict__ meta) {
+// Edge record of one window (floats): a header of kEdgeHeader floats
+// holding int64 {head_seg, head_ends, tail_seg, 0}, then the head piece and
+// the tail piece, W * d floats each (W = 2 for sum: s then c; 1 for max),
+// padded to a multiple of 16 bytes.
+constexpr int kEdgeHeader = 8;
+
+// Floats between consecutive ranks' records: the record rounded up to 16
+// bytes, so that every gathered record starts 16-byte aligned.
+__host__ __device__ __forceinline__ int64_t edge_record_floats(int64_t width_times_d) {
+  return (kEdgeHeader + 2 * width_times_d + 3) / 4 * 4;
+}
+
+template <int OP, int VEC>
+__device__ __forceinline__ void chain_merge(RowAcc<OP, VEC> &total, const float *__restrict__ pieces,
+                                            const UnitMeta *__restrict__ meta, int64_t d, int64_t col, bool active,
+                                            int64_t lo, int64_t hi, bool head_at_hi, float (*s_part)[2][32 * VEC]) {
+  // Slot-1 pieces (TAIL / THROUGH) of CTAs [lo, hi), then the HEAD (slot 0)
+  // of CTA hi when head_at_hi.  Result in `total` of warp 0's lanes.
   using Acc = RowAcc<OP, VEC>;
   constexpr int NW = kFixupThreads / 32;
-  const int64_t u = blockIdx.x;
-  if (meta[u].tail_kind != PIECE_TAIL) return;  // uniform across the CTA
-  const int64_t seg = meta[u].tail_seg;
-  __shared__ int64_t s_end;
-  __shared__ float s_part[NW][2][32 * VEC];  // per-warp partials: (s, c) or (m)
-  if (threadIdx.x == 0) s_end = INT64_MAX;
-  __syncthreads();
-  for (int64_t base = u + 1; base < units; base += kFixupThreads) {
-    const int64_t v = base + threadIdx.x;
-    if (v < units && meta[v].head_seg == seg) atomicMin(reinterpret_cast<unsigned long long *>(&s_end),
-                                                        static_cast<unsigned long long>(v));
-    __syncthreads();
-    if (s_end != INT64_MAX) break;  // uniform: read after the barrier
-    __syncthreads();
-  }
-  const int64_t end = s_end;  // the HEAD unit: the segment's end is consumed by a later unit
-  if (end >= units) return;   // unreachable for valid offsets; never read past the metadata
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int cv = blockIdx.y * 32 + lane;
-  const bool active = cv < vec_cols;
-  const int64_t col = static_cast<int64_t>(cv) * VEC;
-  const int64_t stride = d;
   const int64_t span = 2 * Acc::kWidth * d;
-  // THROUGH pieces of CTAs (u, end): warp w takes a contiguous run, four
-  // entries per step with independent loads.
-  const int64_t first = u + 1, count = end > first ? end - first : 0;
+  const int64_t count = hi > lo ? hi - lo : 0;
   const int64_t per = (count + NW - 1) / NW;
-  const int64_t lo = first + warp * per, hi = lo + per < end ? lo + per : end;
+  const int64_t a = lo + warp * per, e = a + per < hi ? a + per : hi;
   Acc acc;
   acc.init();
   if (active) {
-    for (int64_t v = lo; v < hi; v += 4) {
+    for (int64_t v = a; v < e; v += 4) {
       int32_t kind[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) kind[i] = v + i < hi ? meta[v + i].tail_kind : PIECE_NONE;
+      for (int i = 0; i < 4; ++i) kind[i] = v + i < e ? meta[v + i].tail_kind : PIECE_NONE;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        if (kind[i] == PIECE_THROUGH) acc.merge_piece(pieces + (v + i) * span + Acc::kWidth * d + col, stride);
+        if (kind[i] != PIECE_NONE) acc.merge_piece(pieces + (v + i) * span + Acc::kWidth * d + col, d);
     }
   }
   if (active) acc.store_piece(&s_part[warp][0][lane * VEC], 32 * VEC);
   __syncthreads();
   if (warp == 0 && active) {
-    Acc total;
-    total.load_piece(pieces + u * span + Acc::kWidth * d + col, stride);
+    total.init();
 #pragma unroll
     for (int w = 0; w < NW; ++w) total.merge_piece(&s_part[w][0][lane * VEC], 32 * VEC);
-    total.merge_piece(pieces + end * span + col, stride);
+    if (head_at_hi) total.merge_piece(pieces + hi * span + col, d);
+  }
+}
+
+// First CTA v in [from, units) whose HEAD piece belongs to `seg`
+// (INT64_MAX if none), scanning kFixupThreads entries per step.
+__device__ __forceinline__ int64_t find_head(const UnitMeta *__restrict__ meta, int64_t from, int64_t units,
+                                             int64_t seg, int64_t *s_end) {
+  if (threadIdx.x == 0) *s_end = INT64_MAX;
+  __syncthreads();
+  for (int64_t base = from; base < units; base += kFixupThreads) {
+    const int64_t v = base + threadIdx.x;
+    if (v < units && meta[v].head_seg == seg)
+      atomicMin(reinterpret_cast<unsigned long long *>(s_end), static_cast<unsigned long long>(v));
+    __syncthreads();
+    if (*s_end != INT64_MAX) break;  // uniform: read after the barrier
+    __syncthreads();
+  }
+  return *s_end;
+}
+
+template <typename T, int OP, int VEC>
+__global__ void __launch_bounds__(kFixupThreads)
+rowbal_fixup_kernel(T *__restrict__ out, int64_t d, int vec_cols, int64_t units,
+                    const float *__restrict__ pieces, const UnitMeta *__restrict__ meta, float *__restrict__ edges) {
+  using Acc = RowAcc<OP, VEC>;
+  constexpr int NW = kFixupThreads / 32;
+  __shared__ int64_t s_end;
+  __shared__ float s_part[NW][2][32 * VEC];  // per-warp partials: (s, c) or (m)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cv = blockIdx.y * 32 + lane;
+  const bool active = cv < vec_cols;
+  const int64_t col = static_cast<int64_t>(cv) * VEC;
+  const int64_t wd = Acc::kWidth * d;
+  const int64_t u = blockIdx.x;
+  Acc total;
+  if (u == units) {
+    // ---- window start (sharded calls only): the segment open at row0
+    const int64_t head0 = meta[0].head_seg;
+    const int64_t seg0 = head0 >= 0 ? head0 : (meta[0].tail_kind == PIECE_THROUGH ? meta[0].tail_seg : -1);
+    int64_t end = INT64_MAX;
+    if (seg0 >= 0) {
+      end = head0 >= 0 ? 0 : find_head(meta, 1, units, seg0, &s_end);
+      const bool ends = end < units;
+      chain_merge<OP, VEC>(total, pieces, meta, d, col, active, 0, ends ? end : units, ends, s_part);
+      if (warp == 0 && active) total.store_piece(edges + kEdgeHeader + col, d);
+    }
+    if (threadIdx.x == 0 && blockIdx.y == 0) {
+      int64_t *hdr = reinterpret_cast<int64_t *>(edges);
+      const bool through = seg0 >= 0 && end >= units;
+      const UnitMeta &last = meta[units - 1];
+      hdr[0] = seg0;
+      hdr[1] = seg0 >= 0 && !through;
+      hdr[2] = (!through && last.tail_kind != PIECE_NONE) ? last.tail_seg : -1;
+      hdr[3] = 0;
+    }
+    return;
+  }
+  if (meta[u].tail_kind != PIECE_TAIL) return;  // uniform across the CTA
+  const int64_t seg = meta[u].tail_seg;
+  const int64_t end = find_head(meta, u + 1, units, seg, &s_end);
+  if (end >= units) {
+    // ---- window end (sharded calls): TAIL and THROUGH pieces, no HEAD
+    if (edges == nullptr) return;  // unreachable for a whole-array call with valid offsets
+    chain_merge<OP, VEC>(total, pieces, meta, d, col, active, u, units, false, s_part);
+    if (warp == 0 && active) total.store_piece(edges + kEdgeHeader + wd + col, d);
+    return;
+  }
+  chain_merge<OP, VEC>(total, pieces, meta, d, col, active, u, end, true, s_part);
+  if (warp == 0 && active) {
     float y[VEC];
     total.value(y);
     VecIO<T, VEC>::store(out + seg * d + col, y);
   }
+}
+
+// Finish the segments cut by shard boundaries on the rank that consumed
+// their end: gathered[k] is rank k's edge record (kEdgeHeader + 2 W d
+// floats).  Rank `rank` owns the segment of its head piece if it consumed
+// that segment's end; the pieces merge in rank order: the starting rank's
+// tail piece, the head pieces of ranks the segment passes through, then
+// this rank's head piece.  One CTA per column tile.
+template <typename T, int OP, int VEC>
+__global__ void __launch_bounds__(32)
+shard_combine_kernel(T *__restrict__ out, int64_t d, int vec_cols, int world, int rank,
+                     const float *__restrict__ gathered) {
+  using Acc = RowAcc<OP, VEC>;
+  const int64_t wd = Acc::kWidth * d;
+  const int64_t rec = edge_record_floats(wd);
+  const int64_t *hdr = reinterpret_cast<const int64_t *>(gathered + rank * rec);
+  const int64_t seg = hdr[0];
+  if (seg < 0 || hdr[1] == 0) return;
+  const int cv = blockIdx.y * 32 + threadIdx.x;
+  if (cv >= vec_cols) return;
+  const int64_t col = static_cast<int64_t>(cv) * VEC;
+  int k = rank - 1;  // walk back over ranks the segment passes through
+  while (k > 0) {
+    const int64_t *h = reinterpret_cast<const int64_t *>(gathered + k * rec);
+    if (h[0] == seg && h[1] == 0) --k;
+    else break;
+  }
+  Acc total;
+  total.init();
+  if (k >= 0) {
+    const int64_t *h = reinterpret_cast<const int64_t *>(gathered + k * rec);
+    if (h[2] == seg) total.merge_piece(gathered + k * rec + kEdgeHeader + wd + col, d);            // tail piece
+    else if (h[0] == seg) total.merge_piece(gathered + k * rec + kEdgeHeader + col, d);            // rank 0 through
+  }
+  for (int j = k + 1; j < rank; ++j) total.merge_piece(gathered + j * rec + kEdgeHeader + col, d);  // through ranks
+  total.merge_piece(gathered + rank * rec + kEdgeHeader + col, d);                                 // this rank's head
+  float y[VEC];
+  total.value(y);
+  VecIO<T, VEC>::store(out + seg * d + col, y);
 }
 
 }  // namespace rgb

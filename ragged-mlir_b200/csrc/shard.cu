@@ -1,0 +1,292 @@
+// Row-sharded sum / max across the GPUs of one node (one process per GPU).
+//
+// Rank r of `world` owns rows [row0, row1) = [r N / world, (r+1) N / world)
+// of the packed values (rg_shard_rows) and holds only those rows; every rank
+// holds the whole offsets array.  rg_run_shard runs the row-balanced kernel
+// over the rank's window of the merge path (rowbal.cuh, RowWindow): the
+// window starts at the diagonal of row0 (rows before it plus the segment
+// ends at or before it) and ends at the diagonal of row1, so the windows of
+// the ranks tile the path and every segment end is consumed by exactly one
+// rank.  A segment that starts and ends inside one window is written there;
+// the segment open at a window's start and the one open at its end leave
+// f32 pieces in the rank's edge record.  The ranks all-gather their edge
+// records (NCCL over NVLink, a few KB per rank: torch.distributed in the
+// Python layer), and rg_shard_combine finishes, on the rank that consumed
+// each cut segment's end, the merge of its pieces in rank order -- so the
+// result does not depend on NCCL's reduction order, max keeps NaN
+// propagation, and each output row is rounded once.
+//
+// No kernel here waits on another rank: the exchange is a collective
+// between two launches.
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "internal.h"
+#include "rowbal.cuh"
+
+namespace rgb {
+
+namespace {
+
+std::mutex g_shard_mutex;
+std::map<std::pair<const void *, int>, int> g_shard_occupancy;
+
+int shard_blocks_per_sm(const void *kernel, int device, int *blocks) {
+  std::lock_guard<std::mutex> lock(g_shard_mutex);
+  const auto key = std::make_pair(kernel, device);
+  auto it = g_shard_occupancy.find(key);
+  if (it == g_shard_occupancy.end()) {
+    int n = 0;
+    const int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kRowbalThreads, 0),
+                                  "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (status) return status;
+    it = g_shard_occupancy.emplace(key, n < 1 ? 1 : n).first;
+  }
+  *blocks = it->second;
+  return RG_OK;
+}
+
+struct ShardPlan {
+  int64_t ctas, units;
+  int64_t pieces_bytes, meta_bytes;
+};
+
+constexpr int64_t kAlign = 256;
+int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// One resident wave of CTAs (per column tile), no more than one unit per 64
+// items of the window's path (bounded by its rows plus all segment ends).
+template <typename T, typename OffT, int OP, int VEC>
+int shard_plan(const Problem &p, const Geometry &g, int64_t rows, ShardPlan *plan) {
+  DeviceProps dev;
+  int status = device_props(&dev);
+  if (status) return status;
+  int per_sm = 0;
+  status = shard_blocks_per_sm(reinterpret_cast<const void *>(&rowbal_kernel<T, OffT, OP, VEC>), dev.device, &per_sm);
+  if (status) return status;
+  const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
+  int64_t ctas = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
+  const int64_t path = rows + p.b;
+  const int64_t wanted = (path + 64 * units_per_cta - 1) / (64 * units_per_cta);
+  if (wanted < ctas) ctas = wanted;
+  if (ctas < 1) ctas = 1;
+  plan->ctas = ctas;
+  plan->units = ctas * units_per_cta;
+  const int width = OP == OP_SUM ? 2 : 1;
+  plan->pieces_bytes = align_up(ctas * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
+  plan->meta_bytes = align_up(ctas * static_cast<int64_t>(sizeof(UnitMeta)));
+  return RG_OK;
+}
+
+struct ShardCall {
+  int64_t row0, row1;
+  int first;
+  float *edges;
+};
+
+template <typename T, typename OffT, int OP, int VEC>
+int shard_typed(const Problem &p, const Geometry &g, const ShardCall &c, void *workspace, int64_t *bytes,
+                cudaStream_t stream, rg_report *report) {
+  ShardPlan plan;
+  int status = shard_plan<T, OffT, OP, VEC>(p, g, c.row1 - c.row0, &plan);
+  if (status) return status;
+  if (bytes) {
+    *bytes = plan.pieces_bytes + plan.meta_bytes;
+    return RG_OK;
+  }
+  float *pieces = static_cast<float *>(workspace);
+  UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
+  dim3 grid(static_cast<unsigned>(plan.ctas), g.col_tiles, 1);
+  rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
+      static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b, p.d,
+      g.g_shift, g.vec_cols, plan.units, pieces, meta, RowWindow{c.row0, c.row1, c.first});
+  record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
+  status = check_cuda(cudaGetLastError(), "rowbal_kernel launch (shard)");
+  if (status) return status;
+  // Every CTA with a TAIL piece, plus one CTA for the window's start and the
+  // edge record's header.
+  dim3 fix_grid(static_cast<unsigned>(plan.ctas + 1), g.col_tiles, 1);
+  rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols,
+                                                                          plan.ctas, pieces, meta, c.edges);
+  record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
+  return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch (shard)");
+}
+
+template <typename T, typename OffT, int OP>
+int shard_vec(const Problem &p, const Geometry &g, const ShardCall &c, void *ws, int64_t *bytes, cudaStream_t s,
+              rg_report *r) {
+  switch (g.vec) {
+    case 1: return shard_typed<T, OffT, OP, 1>(p, g, c, ws, bytes, s, r);
+    case 2: return shard_typed<T, OffT, OP, 2>(p, g, c, ws, bytes, s, r);
+    case 4: return shard_typed<T, OffT, OP, 4>(p, g, c, ws, bytes, s, r);
+    case 8:
+      if constexpr (sizeof(T) == 2) return shard_typed<T, OffT, OP, 8>(p, g, c, ws, bytes, s, r);
+      break;
+  }
+  return fail(RG_ERR_INVALID_ARGUMENT, "unsupported vector width");
+}
+
+template <typename T>
+int shard_dispatch(const Problem &p, const Geometry &g, const ShardCall &c, void *ws, int64_t *bytes, cudaStream_t s,
+                   rg_report *r) {
+  const bool i32 = p.index_dtype == RG_INDEX_I32;
+  if (p.op == RG_OP_SUM)
+    return i32 ? shard_vec<T, int32_t, OP_SUM>(p, g, c, ws, bytes, s, r) : shard_vec<T, int64_t, OP_SUM>(p, g, c, ws, bytes, s, r);
+  return i32 ? shard_vec<T, int32_t, OP_MAX>(p, g, c, ws, bytes, s, r) : shard_vec<T, int64_t, OP_MAX>(p, g, c, ws, bytes, s, r);
+}
+
+int shard_run(const Problem &p, const Geometry &g, const ShardCall &c, void *ws, int64_t *bytes, cudaStream_t s,
+              rg_report *r) {
+  return p.dtype == RG_DTYPE_F32 ? shard_dispatch<float>(p, g, c, ws, bytes, s, r)
+                                 : shard_dispatch<__nv_bfloat16>(p, g, c, ws, bytes, s, r);
+}
+
+template <typename T, int OP>
+int combine_typed(const Geometry &g, int64_t d, int world, int rank, const float *gathered, T *out, cudaStream_t s) {
+  dim3 grid(1, g.col_tiles, 1);
+  switch (g.vec) {
+    case 1: shard_combine_kernel<T, OP, 1><<<grid, 32, 0, s>>>(out, d, g.vec_cols, world, rank, gathered); break;
+    case 2: shard_combine_kernel<T, OP, 2><<<grid, 32, 0, s>>>(out, d, g.vec_cols, world, rank, gathered); break;
+    case 4: shard_combine_kernel<T, OP, 4><<<grid, 32, 0, s>>>(out, d, g.vec_cols, world, rank, gathered); break;
+    case 8:
+      if constexpr (sizeof(T) == 2) {
+        shard_combine_kernel<T, OP, 8><<<grid, 32, 0, s>>>(out, d, g.vec_cols, world, rank, gathered);
+        break;
+      }
+      return fail(RG_ERR_INVALID_ARGUMENT, "unsupported vector width");
+    default: return fail(RG_ERR_INVALID_ARGUMENT, "unsupported vector width");
+  }
+  return check_cuda(cudaGetLastError(), "shard_combine_kernel launch");
+}
+
+// Op and split checks shared by the shard entry points; the rank's rows.
+int shard_window(int op, int64_t n, int world, int rank, int64_t *row0, int64_t *row1) {
+  if (op != RG_OP_SUM && op != RG_OP_MAX)
+    return fail(RG_ERR_UNSUPPORTED, "sharded calls compute sum and max (softmax is single-GPU in this build)");
+  if (n < 0 || world < 1 || rank < 0 || rank >= world)
+    return fail(RG_ERR_INVALID_ARGUMENT, "need N >= 0, world >= 1 and 0 <= rank < world");
+  const int64_t q = n / world, rem = n % world;
+  *row0 = q * rank + (rank < rem ? rank : rem);
+  *row1 = *row0 + q + (rank < rem ? 1 : 0);
+  return RG_OK;
+}
+
+}  // namespace
+
+}  // namespace rgb
+
+using namespace rgb;
+
+extern "C" {
+
+int rg_shard_rows(int64_t n, int world, int rank, int64_t *row0, int64_t *row1) {
+  if (!row0 || !row1) return fail(RG_ERR_INVALID_ARGUMENT, "row0 and row1 must not be NULL");
+  if (n < 0 || world < 1 || rank < 0 || rank >= world)
+    return fail(RG_ERR_INVALID_ARGUMENT, "need N >= 0, world >= 1 and 0 <= rank < world");
+  // Row-balanced split; n / world * r + min(r, n % world) avoids overflow.
+  return shard_window(RG_OP_SUM, n, world, rank, row0, row1);
+}
+
+int rg_shard_edge_bytes(int op, int64_t d, int64_t *bytes) {
+  if (!bytes) return fail(RG_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  if (d < 1 || d > 1024) return fail(RG_ERR_INVALID_ARGUMENT, "D must lie in [1, 1024]");
+  if (op != RG_OP_SUM && op != RG_OP_MAX) return fail(RG_ERR_UNSUPPORTED, "sharded calls compute sum and max");
+  const int64_t width = op == RG_OP_SUM ? 2 : 1;
+  *bytes = edge_record_floats(width * d) * static_cast<int64_t>(sizeof(float));
+  return RG_OK;
+}
+
+int rg_shard_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world,
+                             int rank, uint32_t flags, int64_t *bytes) {
+  if (!bytes) return fail(RG_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  int64_t row0 = 0, row1 = 0;
+  int status = shard_window(op, n, world, rank, &row0, &row1);
+  if (status) return status;
+  Problem p{op, dtype, index_dtype, d, n, b, nullptr, nullptr, nullptr, -1, flags};
+  if ((dtype != RG_DTYPE_F32 && dtype != RG_DTYPE_BF16) || (index_dtype != RG_INDEX_I32 && index_dtype != RG_INDEX_I64) ||
+      d < 1 || d > 1024 || b < 0)
+    return fail(RG_ERR_INVALID_ARGUMENT, "invalid problem description");
+  if (b == 0) {
+    *bytes = 0;
+    return RG_OK;
+  }
+  DeviceProps dev;
+  status = check_device(&dev);
+  if (status) return status;
+  return shard_run(p, make_geometry(p), ShardCall{row0, row1, rank == 0, nullptr}, nullptr, bytes, nullptr, nullptr);
+}
+
+int rg_run_shard(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world, int rank,
+                 const void *values, const void *offsets, void *out, void *edges, void *workspace,
+                 int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report) {
+  if (report) {
+    std::memset(report, 0, sizeof *report);
+    report->schedule = RG_SCHEDULE_ROWBALANCED;
+    report->streams = 1;
+  }
+  int64_t row0 = 0, row1 = 0;
+  int status = shard_window(op, n, world, rank, &row0, &row1);
+  if (status) return status;
+  // The local tensors: values holds the window's rows, out all B rows.
+  Problem local{op, dtype, index_dtype, d, row1 - row0, b, values, offsets, out, -1, flags};
+  if (index_dtype == RG_INDEX_I32 && n > 2147483647LL) return fail(RG_ERR_INVALID_ARGUMENT, "N exceeds the i32 offsets range");
+  if (b == 0 && n != 0) return fail(RG_ERR_INVALID_ARGUMENT, "B=0 requires N=0");
+  if (b > 0) {
+    status = validate(local);
+    if (status) return status;
+  }
+  if (!edges) return fail(RG_ERR_INVALID_ARGUMENT, "edges must hold rg_shard_edge_bytes() bytes of device memory");
+  if (reinterpret_cast<uintptr_t>(edges) % 16) return fail(RG_ERR_INVALID_ARGUMENT, "edges must be 16-byte aligned");
+  const Geometry g = make_geometry(local);
+  if (report) {
+    report->d_vector = g.vec;
+    report->d_tile = 1 << g.g_shift;
+  }
+  DeviceProps dev;
+  status = check_device(&dev);
+  if (status) return status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Problem p{op, dtype, index_dtype, d, n, b, values, offsets, out, -1, flags};
+  if (b == 0) {
+    // No segments: an all-ones header (every field -1) says "nothing cut".
+    return check_cuda(cudaMemsetAsync(edges, 0xff, kEdgeHeader * sizeof(float), s), "cudaMemsetAsync (edges)");
+  }
+  int64_t need = 0;
+  status = shard_run(p, g, ShardCall{row0, row1, rank == 0, nullptr}, nullptr, &need, nullptr, nullptr);
+  if (status) return status;
+  if (report) report->workspace_bytes = need;
+  if (!workspace || workspace_bytes < need) return fail(RG_ERR_WORKSPACE, "workspace missing or too small");
+  if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(RG_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  return shard_run(p, g, ShardCall{row0, row1, rank == 0, static_cast<float *>(edges)}, workspace, nullptr, s, report);
+}
+
+int rg_shard_combine(int op, int dtype, int64_t d, int world, int rank, const void *gathered, void *out,
+                     uint32_t flags, void *stream) {
+  if (op != RG_OP_SUM && op != RG_OP_MAX) return fail(RG_ERR_UNSUPPORTED, "sharded calls compute sum and max");
+  if (dtype != RG_DTYPE_F32 && dtype != RG_DTYPE_BF16) return fail(RG_ERR_INVALID_ARGUMENT, "dtype must be f32 or bf16");
+  if (d < 1 || d > 1024) return fail(RG_ERR_INVALID_ARGUMENT, "D must lie in [1, 1024]");
+  if (world < 1 || rank < 0 || rank >= world) return fail(RG_ERR_INVALID_ARGUMENT, "need 0 <= rank < world");
+  if (!gathered || !out) return fail(RG_ERR_INVALID_ARGUMENT, "gathered and out must not be NULL");
+  if (rank == 0) return RG_OK;  // rank 0 has no segment open at its start
+  DeviceProps dev;
+  int status = check_device(&dev);
+  if (status) return status;
+  Problem p{op, dtype, RG_INDEX_I64, d, 0, 1, nullptr, nullptr, out, -1, flags};
+  const Geometry g = make_geometry(p);
+  if (reinterpret_cast<uintptr_t>(out) % (g.vec * elem_bytes(dtype)))
+    return fail(RG_ERR_INVALID_ARGUMENT, "out is not aligned for this call's vector width");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float *gath = static_cast<const float *>(gathered);
+  if (dtype == RG_DTYPE_F32) {
+    return op == RG_OP_SUM ? combine_typed<float, OP_SUM>(g, d, world, rank, gath, static_cast<float *>(out), s)
+                           : combine_typed<float, OP_MAX>(g, d, world, rank, gath, static_cast<float *>(out), s);
+  }
+  return op == RG_OP_SUM
+             ? combine_typed<__nv_bfloat16, OP_SUM>(g, d, world, rank, gath, static_cast<__nv_bfloat16 *>(out), s)
+             : combine_typed<__nv_bfloat16, OP_MAX>(g, d, world, rank, gath, static_cast<__nv_bfloat16 *>(out), s);
+}
+
+}  // extern "C"

@@ -29,7 +29,8 @@ MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.
 EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
-            "rg_run", "rg_kernel_name", "rg_run_noalloc")
+            "rg_run", "rg_kernel_name", "rg_shard_rows", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
+            "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
 
 
 class Report(ctypes.Structure):
@@ -81,6 +82,18 @@ def library(path: Path | None = None):
         lib.rg_run.restype = i32
         lib.rg_run_noalloc.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, u32, p]
         lib.rg_run_noalloc.restype = i32
+        pi64 = ctypes.POINTER(i64)
+        lib.rg_shard_rows.argtypes = [i64, i32, i32, pi64, pi64]
+        lib.rg_shard_rows.restype = i32
+        lib.rg_shard_edge_bytes.argtypes = [i32, i64, pi64]
+        lib.rg_shard_edge_bytes.restype = i32
+        lib.rg_shard_workspace_bytes.argtypes = [i32, i32, i32, i64, i64, i64, i32, i32, u32, pi64]
+        lib.rg_shard_workspace_bytes.restype = i32
+        lib.rg_run_shard.argtypes = [i32, i32, i32, i64, i64, i64, i32, i32, p, p, p, p, p, i64, u32, p,
+                                     ctypes.POINTER(Report)]
+        lib.rg_run_shard.restype = i32
+        lib.rg_shard_combine.argtypes = [i32, i32, i64, i32, i32, p, p, u32, p]
+        lib.rg_shard_combine.restype = i32
         _lib = lib
         return lib
 
@@ -136,3 +149,43 @@ def run(op: str, dtype: str, index: str, d: int, n: int, b: int, values_ptr: int
                               -1 if max_len is None else max_len, flags, stream or None, ctypes.byref(report))
     raise_for(status, "rg_run")
     return report
+
+
+# ------------------------------------------------------------ sharded calls
+
+def shard_rows(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [row0, row1) of ``rank`` in the row-balanced split of ``n`` rows."""
+    row0, row1 = ctypes.c_int64(0), ctypes.c_int64(0)
+    raise_for(library().rg_shard_rows(n, world, rank, ctypes.byref(row0), ctypes.byref(row1)), "rg_shard_rows")
+    return int(row0.value), int(row1.value)
+
+
+def shard_edge_bytes(op: str, d: int) -> int:
+    out = ctypes.c_int64(0)
+    raise_for(library().rg_shard_edge_bytes(OPS[op], d, ctypes.byref(out)), "rg_shard_edge_bytes")
+    return int(out.value)
+
+
+def shard_workspace_bytes(op: str, dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int,
+                          flags: int = 0) -> int:
+    out = ctypes.c_int64(0)
+    raise_for(library().rg_shard_workspace_bytes(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank, flags,
+                                                 ctypes.byref(out)), "rg_shard_workspace_bytes")
+    return int(out.value)
+
+
+def run_shard(op: str, dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int, values_ptr: int,
+              offsets_ptr: int, out_ptr: int, edges_ptr: int, workspace_ptr: int, workspace_bytes: int, flags: int,
+              stream: int) -> Report:
+    report = Report()
+    status = library().rg_run_shard(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank, values_ptr or None,
+                                    offsets_ptr, out_ptr, edges_ptr, workspace_ptr or None, workspace_bytes, flags,
+                                    stream or None, ctypes.byref(report))
+    raise_for(status, "rg_run_shard")
+    return report
+
+
+def shard_combine(op: str, dtype: str, d: int, world: int, rank: int, gathered_ptr: int, out_ptr: int, flags: int,
+                  stream: int) -> None:
+    raise_for(library().rg_shard_combine(OPS[op], DTYPES[dtype], d, world, rank, gathered_ptr, out_ptr, flags,
+                                         stream or None), "rg_shard_combine")

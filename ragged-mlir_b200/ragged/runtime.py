@@ -227,6 +227,62 @@ class CompiledProgram:
                                  max_len, self._flags, active.cuda_stream)
         return self._report(schedule, selection, started, report, nbytes)
 
+    def run_sharded(self, values, offsets, out, *, total_rows: int, world: int, rank: int, exchange,
+                    stream=None) -> ExecutionReport:
+        """One rank's part of a row-sharded sum or max (``ragged.sharding``).
+
+        ``values`` holds this rank's rows ``sharding.shard_rows(total_rows,
+        world, rank)`` of a call over ``total_rows`` rows, ``offsets`` all B+1
+        entries, ``out`` all B
+        output rows (only the rows this rank finishes are written:
+        ``sharding.segment_owners``).  ``exchange(edges)`` must return the
+        edge records of ranks 0..world-1 concatenated (an all-gather); it is
+        the only communication.  Launches on ``stream`` (default: current),
+        no host synchronisation of its own."""
+        if self.spec.op not in ("sum", "max"):
+            raise RuntimeUnavailable("sharded calls compute sum and max in this build")
+        torch = _torch()
+        if not 0 <= rank < world:
+            raise ValidationError("need 0 <= rank < world")
+        row0, row1 = _native.shard_rows(total_rows, world, rank)
+        for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
+            if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
+                raise RuntimeUnavailable(f"{name} must be a CUDA tensor; no CPU execution fallback exists")
+            if not tensor.is_contiguous():
+                raise ValidationError(f"{name} must be row-major contiguous")
+        d = self.spec.feature_dim
+        b = offsets.numel() - 1
+        if tuple(values.shape) != (row1 - row0, d):
+            raise ValidationError(f"values must hold this rank's {row1 - row0} rows: shape ({row1 - row0}, {d})")
+        if tuple(out.shape) != (b, d):
+            raise ValidationError(f"out shape must be ({b}, {d})")
+        dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype]
+        offset_dtype = {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype]
+        if values.dtype != dtype or out.dtype != dtype or offsets.dtype != offset_dtype:
+            raise ValidationError("tensor dtype differs from compiled dtype/offsets specialization")
+        started = time.perf_counter()
+        with torch.cuda.device(values.device):
+            active = stream if stream is not None else torch.cuda.current_stream(values.device)
+            spec = self.spec
+            nbytes = _native.shard_workspace_bytes(spec.op, spec.dtype, spec.offsets_dtype, d, total_rows, b, world,
+                                                   rank, self._flags)
+            with torch.cuda.stream(active):
+                scratch = torch.empty((max(nbytes, 1),), dtype=torch.uint8, device=values.device)
+                edges = torch.empty((_native.shard_edge_bytes(spec.op, d) // 4,), dtype=torch.float32,
+                                    device=values.device)
+                report = _native.run_shard(spec.op, spec.dtype, spec.offsets_dtype, d, total_rows, b, world, rank,
+                                           values.data_ptr() if values.numel() else 0, offsets.data_ptr(),
+                                           out.data_ptr(), edges.data_ptr(), scratch.data_ptr(), nbytes, self._flags,
+                                           active.cuda_stream)
+                gathered = exchange(edges)
+                if gathered.numel() != world * edges.numel() or gathered.device != values.device:
+                    raise ValidationError("exchange must return every rank's edge record on this device")
+                _native.shard_combine(spec.op, spec.dtype, d, world, rank, gathered.data_ptr(), out.data_ptr(),
+                                      self._flags, active.cuda_stream)
+        result = self._report("rowbalanced", {"sharded": {"world": world, "rank": rank, "rows": [row0, row1]}},
+                              started, report, nbytes)
+        return result
+
     def _report(self, schedule, selection, started, report, nbytes) -> ExecutionReport:
         thresholds = THRESHOLDS if schedule == "classified" else ()
         if report is None:

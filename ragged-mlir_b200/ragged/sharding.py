@@ -1,0 +1,75 @@
+"""Row-sharded calls across the GPUs of one node (one process per GPU).
+
+The reference runs one program on one device (README.md:457-461); this
+build adds a sharded form of the row-balanced sum and max for inputs that
+are spread over several GPUs.  Rank r of ``world`` holds rows
+``shard_rows(N, world, r)`` of the packed values and the whole offsets
+array.  Every rank reduces its rows; a segment cut by a shard boundary
+leaves f32 pieces in the rank's edge record; the ranks all-gather the
+records (NCCL over NVLink through ``torch.distributed``: a few KB per rank,
+the only collective of the path); and the rank that holds a cut segment's
+end merges its pieces in rank order.  Each output row is written by exactly
+one rank: ``segment_owners`` says which.
+
+``ShardedProgram`` wraps a compiled sum or max program for one rank;
+``CompiledProgram.run_sharded`` is the call it makes.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any, Callable
+
+import numpy as np
+
+from .errors import ValidationError
+
+
+def shard_rows(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [row0, row1) of ``rank`` in the row-balanced split of ``n``
+    rows (the split libragged_b200's rg_shard_rows computes)."""
+    if n < 0 or world < 1 or not 0 <= rank < world:
+        raise ValidationError("need n >= 0, world >= 1 and 0 <= rank < world")
+    q, rem = divmod(n, world)
+    row0 = q * rank + min(rank, rem)
+    return row0, row0 + q + (1 if rank < rem else 0)
+
+
+def segment_owners(offsets: np.ndarray, world: int) -> np.ndarray:
+    """Rank that writes each segment's output row: the rank whose rows
+    hold the segment's end (segments ending at row 0 belong to rank 0)."""
+    offsets = np.asarray(offsets, dtype=np.int64)
+    n = int(offsets[-1])
+    ends = np.array([shard_rows(n, world, r)[1] for r in range(world)], dtype=np.int64)
+    return np.searchsorted(ends, offsets[1:], side="left").astype(np.int64)
+
+
+def torch_exchange(group=None) -> Callable[[Any], Any]:
+    """All-gather of edge records over ``group`` (torch.distributed; NCCL on
+    GPUs): returns the records of ranks 0..world-1 concatenated."""
+    import torch
+    import torch.distributed as dist
+
+    def exchange(edges):
+        world = dist.get_world_size(group)
+        gathered = torch.empty((world * edges.numel(),), dtype=edges.dtype, device=edges.device)
+        dist.all_gather_into_tensor(gathered, edges, group=group)
+        return gathered
+
+    return exchange
+
+
+@dataclass
+class ShardedProgram:
+    """A sum or max program bound to one rank of a row-sharded call."""
+
+    program: Any
+    world: int
+    rank: int
+    group: Any = None
+
+    def rows(self, n: int) -> tuple[int, int]:
+        return shard_rows(n, self.world, self.rank)
+
+    def run(self, values, offsets, out, *, total_rows: int, stream=None):
+        return self.program.run_sharded(values, offsets, out, total_rows=total_rows, world=self.world, rank=self.rank,
+                                        exchange=torch_exchange(self.group), stream=stream)

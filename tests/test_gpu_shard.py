@@ -1,0 +1,120 @@
+"""Row-sharded sum / max through the C ABI, ranks emulated on one GPU.
+
+Every rank of a ``world``-way split runs ``rg_run_shard`` on its own rows;
+their edge records are gathered in rank order, then every rank runs
+``rg_shard_combine``.  No kernel waits on another rank, so running the ranks
+one after another on one device is the same computation as one process per
+GPU with an all-gather in between.  The assembled output (each row from the
+rank ``segment_owners`` names) must match the CPU oracle, and every rank
+must leave the rows it does not own untouched.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from helpers import SENTINEL, check, make_lengths, offsets_of, prepared
+from oracle import reference_port as rp
+
+pytestmark = pytest.mark.gpu
+
+
+def run_world(torch, op, dtype, values, offsets, world):
+    from ragged import _native
+    from ragged.sharding import segment_owners, shard_rows
+    d = values.shape[1]
+    n, b = int(offsets[-1]), offsets.size - 1
+    index = "i32" if offsets.dtype == np.int32 else "i64"
+    tdtype = torch.float32 if dtype == "f32" else torch.bfloat16
+    dev_values = torch.from_numpy(np.ascontiguousarray(values, dtype=np.float32)).to("cuda").to(tdtype)
+    dev_offsets = torch.from_numpy(offsets).to("cuda")
+    edge_floats = _native.shard_edge_bytes(op, d) // 4
+    edges = torch.empty((world, edge_floats), dtype=torch.float32, device="cuda")
+    outs = []
+    for rank in range(world):
+        row0, row1 = shard_rows(n, world, rank)
+        assert (row0, row1) == _native.shard_rows(n, world, rank)
+        local = dev_values[row0:row1].contiguous()
+        out = torch.full((b, d), SENTINEL, dtype=tdtype, device="cuda")
+        ws = _native.shard_workspace_bytes(op, dtype, index, d, n, b, world, rank)
+        scratch = torch.empty((max(ws, 1),), dtype=torch.uint8, device="cuda")
+        _native.run_shard(op, dtype, index, d, n, b, world, rank, local.data_ptr() if local.numel() else 0,
+                          dev_offsets.data_ptr(), out.data_ptr(), edges[rank].data_ptr(), scratch.data_ptr(), ws, 0,
+                          torch.cuda.current_stream().cuda_stream)
+        outs.append(out)
+    gathered = edges.reshape(-1).contiguous()
+    for rank in range(world):
+        _native.shard_combine(op, dtype, d, world, rank, gathered.data_ptr(), outs[rank].data_ptr(), 0,
+                              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    owners = segment_owners(offsets, world)
+    host = [o.float().cpu().numpy().astype(np.float64) for o in outs]
+    result = np.empty((b, d), dtype=np.float64)
+    for rank in range(world):
+        mine = owners == rank
+        result[mine] = host[rank][mine]
+        untouched = host[rank][~mine]
+        assert np.all(untouched == SENTINEL), f"rank {rank} wrote rows it does not own"
+    return result
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("dtype,d", [("f32", 128), ("bf16", 256), ("f32", 3), ("bf16", 1024)])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_sharded_matches_oracle(cuda, op, dtype, d, world):
+    rng = np.random.default_rng(1000 + world + d)
+    lengths = make_lengths("long_tail", 400, 60_000 if d <= 256 else 12_000, seed=world)
+    lengths[5] = 0
+    lengths[-1] = 0
+    offsets = offsets_of(lengths)
+    values = prepared(rng.normal(size=(int(offsets[-1]), d)), dtype)
+    if op == "max":
+        values[rng.random(values.shape) < 1e-3] = np.nan
+    actual = run_world(cuda, op, dtype, values, offsets, world)
+    check(actual, values, offsets, op, dtype)
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+def test_sharded_giant_segment_spans_ranks(cuda, op):
+    """One segment through several whole shards (ranks whose rows lie
+    inside it), segments ending exactly on shard boundaries, and empty
+    segments at the boundaries."""
+    world = 5
+    n = 50_000
+    ends = [shard_end for shard_end in (10_000, 20_000, 30_000, 40_000)]
+    lengths = [3, ends[0] - 3, 0, 0, 7, n - ends[0] - 7 - 11, 11, 0]
+    offsets = offsets_of(np.array(lengths, dtype=np.int64))
+    assert offsets[-1] == n
+    values = prepared(np.random.default_rng(7).normal(size=(n, 64)), "f32")
+    actual = run_world(cuda, op, "f32", values, offsets, world)
+    check(actual, values, offsets, op, "f32")
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_no_rows(cuda, world):
+    """N = 0: every segment is empty and ends at row 0; rank 0 writes them."""
+    offsets = np.array([0, 0, 0], dtype=np.int64)
+    values = np.zeros((0, 4), dtype=np.float32)
+    for op in ("sum", "max"):
+        actual = run_world(cuda, op, "f32", values, offsets, world)
+        check(actual, values, offsets, op, "f32")
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_more_ranks_than_rows(cuda, world):
+    lengths = np.array([0, 1, 0, 2, 0], dtype=np.int64)
+    offsets = offsets_of(lengths, "i32")
+    values = prepared(np.arange(3 * 8, dtype=np.float32).reshape(3, 8), "f32")
+    for op in ("sum", "max"):
+        actual = run_world(cuda, op, "f32", values, offsets, world + 3)
+        check(actual, values, offsets, op, "f32")
+
+
+def test_sharded_i32_bimodal_and_determinism(cuda):
+    lengths = make_lengths("bimodal", 3000, 200_000, seed=8)
+    offsets = offsets_of(lengths, "i32")
+    values = prepared(np.random.default_rng(9).normal(size=(int(offsets[-1]), 32)), "bf16")
+    first = run_world(cuda, "sum", "bf16", values, offsets, 4)
+    again = run_world(cuda, "sum", "bf16", values, offsets, 4)
+    np.testing.assert_array_equal(first, again)
+    check(first, values, offsets, "sum", "bf16")

@@ -1,0 +1,172 @@
+"""The multi-GPU sharding protocol on CPU ranks (gloo, world sizes 2 and 3).
+
+Each rank restates, in float64 NumPy, what rg_run_shard and rg_shard_combine
+do on its GPU: it owns rows ``shard_rows(N, world, rank)``; it finishes the
+segments whose end lies in its rows (ends in (row0, row1], or [0, row1] on
+rank 0) and that started there; it publishes an edge record with the piece of
+the segment open at its start (``head``) and the one open at its end
+(``tail``); the records are all-gathered (gloo here, NCCL on GPUs); and the
+rank that consumed a cut segment's end merges the pieces in rank order.  The
+union of what the ranks write must be every segment exactly once and equal
+the oracle.  The shard split must match libragged_b200's rg_shard_rows
+(callable without a GPU).
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from helpers import make_lengths, offsets_of
+
+HEADER = 3  # head_seg, head_ends, tail_seg
+
+
+def _reduce(op, rows):
+    if rows.shape[0] == 0:
+        return np.zeros(rows.shape[1]) if op == "sum" else np.full(rows.shape[1], -np.inf)
+    if op == "sum":
+        return rows.sum(axis=0)
+    out = rows.max(axis=0)
+    out[np.isnan(rows).any(axis=0)] = np.nan
+    return out
+
+
+def _merge(op, a, b):
+    if op == "sum":
+        return a + b
+    out = np.maximum(a, b)
+    out[np.isnan(a) | np.isnan(b)] = np.nan
+    return out
+
+
+def rank_part(op, values_local, offsets, row0, row1, rank):
+    """(finished {segment: row}, edge record) of one rank's window."""
+    b = offsets.size - 1
+    ends = offsets[1:]
+    lo = 0 if rank == 0 else int(np.searchsorted(ends, row0, side="right"))  # first end consumed here
+    hi = int(np.searchsorted(ends, row1, side="right"))                       # ends <= row1
+    finished, head_seg, head_ends, head = {}, -1, 0, None
+    for s in range(lo, hi):
+        start, end = int(offsets[s]), int(offsets[s + 1])
+        rows = values_local[max(start, row0) - row0:end - row0]
+        if start >= row0:
+            finished[s] = _reduce(op, rows)
+        else:  # started on an earlier rank: this rank holds its head piece
+            head_seg, head_ends, head = s, 1, _reduce(op, rows)
+    tail_seg, tail = -1, None
+    if hi < b and row1 > row0:
+        s = hi  # the segment open at row1 (its end lies beyond)
+        start = int(offsets[s])
+        if start < row1:
+            rows = values_local[max(start, row0) - row0:row1 - row0]
+            if start >= row0:
+                tail_seg, tail = s, _reduce(op, rows)
+            elif head_seg < 0:  # through: the segment covers the whole window
+                head_seg, head_ends, head = s, 0, _reduce(op, rows)
+    d = values_local.shape[1]
+    ident = np.zeros(d) if op == "sum" else np.full(d, -np.inf)
+    record = np.concatenate([[head_seg, head_ends, tail_seg],
+                             head if head is not None else ident, tail if tail is not None else ident])
+    return finished, record
+
+
+def combine(op, records, rank, d):
+    """The segment this rank finishes from the gathered records, or None."""
+    head_seg, head_ends = int(records[rank][0]), int(records[rank][1])
+    if head_seg < 0 or head_ends == 0:
+        return None
+    k = rank - 1
+    while k > 0 and int(records[k][0]) == head_seg and int(records[k][1]) == 0:
+        k -= 1
+    head = lambda j: records[j][HEADER:HEADER + d]
+    tail = lambda j: records[j][HEADER + d:]
+    total = tail(k) if int(records[k][2]) == head_seg else head(k)
+    for j in range(k + 1, rank):
+        total = _merge(op, total, head(j))
+    return head_seg, _merge(op, total, head(rank))
+
+
+def _worker(rank, world, port, cases, results):
+    import torch
+    import torch.distributed as dist
+    from ragged.sharding import shard_rows
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        out = []
+        for op, values, offsets in cases:
+            n = int(offsets[-1])
+            row0, row1 = shard_rows(n, world, rank)
+            finished, record = rank_part(op, values[row0:row1], offsets, row0, row1, rank)
+            mine = torch.from_numpy(record)
+            gathered = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(gathered, mine)
+            extra = combine(op, [g.numpy() for g in gathered], rank, values.shape[1])
+            if extra is not None:
+                finished[extra[0]] = extra[1]
+            out.append(finished)
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cases():
+    rng = np.random.default_rng(5)
+    cases = []
+    for op in ("sum", "max"):
+        lengths = make_lengths("long_tail", 60, 5000, seed=3)
+        offsets = offsets_of(lengths)
+        cases.append((op, rng.normal(size=(int(offsets[-1]), 4)), offsets))
+        # A segment through whole shards, ends on shard boundaries, empty segments there.
+        lengths = np.array([0, 3, 997, 0, 0, 1500, 498, 2, 0], dtype=np.int64)
+        offsets = offsets_of(lengths)
+        values = rng.normal(size=(int(offsets[-1]), 3))
+        values[10, 1] = np.nan
+        cases.append((op, values, offsets))
+        cases.append((op, rng.normal(size=(2, 2)), np.array([0, 0, 2, 2], dtype=np.int64)))  # more ranks than rows
+    return cases
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharding_protocol_over_gloo(world):
+    import torch.multiprocessing as mp
+    from oracle import reference_port as rp
+    from ragged.sharding import segment_owners
+    cases = _cases()
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), cases, results), nprocs=world, start_method="spawn")
+    for i, (op, values, offsets) in enumerate(cases):
+        owners = segment_owners(offsets, world)
+        seen = {}
+        for rank in range(world):
+            for s, row in results[rank][i].items():
+                assert s not in seen, f"segment {s} written twice"
+                assert owners[s] == rank, f"segment {s} written by rank {rank}, owner {owners[s]}"
+                seen[s] = row
+        assert sorted(seen) == list(range(offsets.size - 1)), "every segment is written exactly once"
+        actual = np.stack([seen[s] for s in range(offsets.size - 1)])
+        with np.errstate(all="ignore"):
+            expected = rp.REFERENCES[op](values, offsets)
+        np.testing.assert_allclose(actual, expected, rtol=1e-12, atol=1e-12, equal_nan=True)
+
+
+def test_shard_rows_matches_native_library():
+    from ragged import _native
+    from ragged.sharding import shard_rows
+    _native.library()
+    for n in (0, 1, 7, 10, 200_000_000, 2**40 + 3):
+        for world in (1, 2, 3, 8):
+            for rank in range(world):
+                assert shard_rows(n, world, rank) == _native.shard_rows(n, world, rank)
+    assert _native.shard_edge_bytes("sum", 256) % 16 == 0 and _native.shard_edge_bytes("max", 3) % 16 == 0
