@@ -242,34 +242,42 @@ def config_dict(w, args, flush) -> dict:
 # ---------------------------------------------------------------- ours ----
 
 def time_calls(torch, fn, steps, warmup, stream, flush=None, dist=None):
-    """Per-step device time (ms) with CUDA events on ``stream``; with
-    ``dist`` every step is bracketed by a barrier and a synchronize, and the
-    per-step time is the maximum over ranks."""
+    """Per-step device time (ms) with CUDA events on ``stream``, the K steps
+    bracketed by a barrier and a synchronize on both sides; with ``dist``
+    the per-step times are the maximum over ranks."""
     for _ in range(warmup):
         if flush is not None:
             flush()
         fn()
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+        torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
         if flush is not None:
             flush()
-        if dist is not None:
-            torch.cuda.synchronize()
-            dist.barrier()
         starts[i].record(stream)
         fn()
         ends[i].record(stream)
-        if dist is not None:
-            torch.cuda.synchronize()
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     if dist is not None:
-        t = torch.tensor(times, dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+        device = torch.device("cuda", torch.cuda.current_device())
+        mine = torch.tensor([statistics.mean(times)], dtype=torch.float64, device=device)
+        every = [torch.empty_like(mine) for _ in range(dist.get_world_size())]
+        dist.all_gather(every, mine)
+        RANK_MS[:] = [round(float(x.item()), 4) for x in every]
+        t = torch.tensor(times, dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         times = t.cpu().tolist()
     return times
+
+
+RANK_MS: list = []  # mean step time of every rank in the last multi-GPU timing
 
 
 def ours(args) -> None:
@@ -351,6 +359,7 @@ def ours(args) -> None:
             "clocks": clocks.summary()}
     if world > 1:
         line["sharding"] = {"rows_per_rank": [list(shard_rows(w.n, world, r)) for r in range(world)],
+                            "rank_ms": list(RANK_MS),
                             "collective": "NCCL all-gather of edge records",
                             "edge_bytes_per_rank": _native_edge_bytes(w)}
     if not args.no_e2e:

@@ -95,7 +95,7 @@ int run_typed(const Problem &p, const Geometry &g, const DeviceProps &dev, void 
   dim3 grid(static_cast<unsigned>(ctas), g.col_tiles, 1);
   rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
-      p.d, g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{0, p.n, 1});
+      p.d, g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{0, p.n, 1}, nullptr);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch (no-alloc)");
   if (status || ctas < 2) return status;
   dim3 fix_grid(static_cast<unsigned>(ctas), g.col_tiles, 1);

@@ -55,14 +55,25 @@ const void *packed_ptr() {
 constexpr int64_t kAlign = 256;
 int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
+// Virtual CTAs per resident CTA of the row-balanced kernel: the kernel's
+// CTAs take virtual CTAs from a counter, so a slower SM takes fewer.  Up
+// to 8, one per 16K path items of a CTA's share: a small call keeps one
+// static wave (a virtual CTA's start, its merge-path searches, is not free).
+int64_t virtual_per_cta(int64_t path, int64_t resident) {
+  const int64_t k = path / (resident * 16384);
+  return k < 1 ? 1 : (k > 8 ? 8 : k);
+}
+
 struct Plan {
-  int64_t units;
-  int ctas;
-  int64_t pieces_bytes, meta_bytes;
+  int64_t packed_ctas;  // packed narrow-row kernel: one static wave
+  int64_t vctas;        // row-balanced kernel: virtual CTAs ...
+  int64_t grid;         // ... taken by this many resident CTAs (per column tile)
+  int64_t pieces_bytes, meta_bytes, counter;  // workspace: pieces, metadata, claim counter
 };
 
-// Units: enough CTAs for one resident wave (per column tile), but no more
-// than one unit per 64 path items.
+// No more than one unit per 64 path items; the packed kernel runs one
+// resident wave, the row-balanced kernel kVirtualPerCta virtual CTAs per
+// resident CTA.
 int make_plan(const Problem &p, const Geometry &g, const void *kernel, const void *packed, Plan *plan) {
   DeviceProps dev;
   int status = device_props(&dev);
@@ -70,23 +81,30 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
   int per_sm = 0;
   status = occupancy(kernel, dev.device, kRowbalThreads, &per_sm);
   if (status) return status;
-  if (packed) {  // size the plan for whichever kernel the call may take
+  const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
+  const int64_t path = p.n + p.b;
+  const int64_t wanted = (path + 64 * units_per_cta - 1) / (64 * units_per_cta);
+  int64_t resident = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
+  if (resident < 1) resident = 1;
+  int64_t vctas = resident * virtual_per_cta(path, resident);
+  if (vctas > wanted) vctas = wanted < 1 ? 1 : wanted;
+  plan->vctas = vctas;
+  plan->grid = resident < vctas ? resident : vctas;
+  plan->packed_ctas = 0;
+  if (packed) {
     int packed_per_sm = 0;
     status = occupancy(packed, dev.device, kRowbalThreads, &packed_per_sm);
     if (status) return status;
-    if (packed_per_sm > per_sm) per_sm = packed_per_sm;
+    const int64_t packed_wanted = (path + 64 * kRowbalThreads - 1) / (64 * kRowbalThreads);
+    int64_t ctas = static_cast<int64_t>(packed_per_sm) * dev.sm_count;
+    if (ctas > packed_wanted) ctas = packed_wanted;
+    plan->packed_ctas = ctas < 1 ? 1 : ctas;
   }
-  const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
-  int64_t ctas = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
-  if (ctas < 1) ctas = 1;
-  const int64_t path = p.n + p.b;
-  const int64_t wanted = (path + 64 * units_per_cta - 1) / (64 * units_per_cta);
-  if (wanted < ctas) ctas = wanted < 1 ? 1 : wanted;
-  plan->ctas = static_cast<int>(ctas);
-  plan->units = ctas * units_per_cta;
+  const int64_t slots = plan->vctas > plan->packed_ctas ? plan->vctas : plan->packed_ctas;
   const int width = p.op == RG_OP_SUM ? 2 : 1;
-  plan->pieces_bytes = align_up(ctas * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
-  plan->meta_bytes = align_up(ctas * static_cast<int64_t>(sizeof(UnitMeta)));
+  plan->pieces_bytes = align_up(slots * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
+  plan->meta_bytes = align_up(slots * static_cast<int64_t>(sizeof(UnitMeta)));
+  plan->counter = plan->pieces_bytes + plan->meta_bytes;
   return RG_OK;
 }
 
@@ -98,50 +116,44 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC>(), packed, &plan);
   if (status) return status;
   if (bytes) {
-    *bytes = plan.pieces_bytes + plan.meta_bytes;
+    *bytes = plan.counter + kAlign;
     return RG_OK;
   }
   float *pieces = static_cast<float *>(workspace);
   UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
   if constexpr (VEC * sizeof(T) < 16) {
     if (packed && reinterpret_cast<uintptr_t>(p.values) % 16 == 0) {
-      dim3 grid(plan.ctas, 1, 1);
+      const int64_t ctas = plan.packed_ctas;
+      dim3 grid(static_cast<unsigned>(ctas), 1, 1);
       rowbal_packed_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, 0, stream>>>(
           static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
-          plan.units, pieces, meta);
+          ctas * kRowbalThreads, pieces, meta);
       record_launch(report, K_ROWBAL_PACKED, grid, kRowbalThreads, 0);
       status = check_cuda(cudaGetLastError(), "rowbal_packed_kernel launch");
-      if (status || plan.ctas < 2) return status;
-      dim3 fix_grid(static_cast<unsigned>(plan.ctas), 1, 1);
+      if (status || ctas < 2) return status;
+      dim3 fix_grid(static_cast<unsigned>(ctas), 1, 1);
       rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d,
-                                                                              g.vec_cols, plan.ctas, pieces, meta, nullptr);
+                                                                              g.vec_cols, ctas, pieces, meta, nullptr);
       record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
       return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
     }
   }
-  int64_t ctas = plan.ctas;  // the unpacked kernel may hold fewer CTAs than the plan sized for
-  {
-    DeviceProps dev;
-    status = device_props(&dev);
-    if (status) return status;
-    int per_sm = 0;
-    status = occupancy(kernel_ptr<T, OffT, OP, VEC>(), dev.device, kRowbalThreads, &per_sm);
-    if (status) return status;
-    const int64_t cap = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
-    if (ctas > cap && cap >= 1) ctas = cap;
-  }
-  plan.ctas = static_cast<int>(ctas);
-  plan.units = ctas * ((kRowbalThreads / 32) << (5 - g.g_shift));
-  dim3 grid(plan.ctas, g.col_tiles, 1);
+  unsigned long long *counter =
+      reinterpret_cast<unsigned long long *>(static_cast<char *>(workspace) + plan.counter);
+  status = check_cuda(cudaMemsetAsync(counter, 0, sizeof *counter, stream), "cudaMemsetAsync");
+  if (status) return status;
+  if (report) report->memsets += 1;
+  const int64_t units = plan.vctas * ((kRowbalThreads / 32) << (5 - g.g_shift));
+  dim3 grid(static_cast<unsigned>(plan.grid), g.col_tiles, 1);
   rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
-      p.d, g.g_shift, g.vec_cols, plan.units, pieces, meta, RowWindow{0, p.n, 1});
+      p.d, g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{0, p.n, 1}, counter);
   record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch");
-  if (status || plan.ctas < 2) return status;
-  dim3 fix_grid(static_cast<unsigned>(plan.ctas), g.col_tiles, 1);
+  if (status || plan.vctas < 2) return status;
+  dim3 fix_grid(static_cast<unsigned>(plan.vctas), g.col_tiles, 1);
   rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols,
-                                                                          plan.ctas, pieces, meta, nullptr);
+                                                                          plan.vctas, pieces, meta, nullptr);
   record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
   return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
 }

@@ -286,7 +286,8 @@ template <typename T, typename OffT, int OP, int VEC, int U = RowbalTuning::kUnr
 __global__ void __launch_bounds__(kRowbalThreads, MINB)
 rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
               int64_t n, int64_t b, int64_t d, int g_shift, int vec_cols, int64_t units,
-              float *__restrict__ pieces, UnitMeta *__restrict__ meta, RowWindow window) {
+              float *__restrict__ pieces, UnitMeta *__restrict__ meta, RowWindow window,
+              unsigned long long *__restrict__ work) {
   using Acc = RowAcc<OP, VEC>;
   const int lane = threadIdx.x & 31;
   const int G = 1 << g_shift;
@@ -296,15 +297,33 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   const unsigned group_mask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << group_base);
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g_shift);
   const int unit_in_cta = (threadIdx.x >> 5) * (32 >> g_shift) + q;
-  const int64_t unit = static_cast<int64_t>(blockIdx.x) * units_per_cta + unit_in_cta;  // < units by construction
-  const int cv = blockIdx.y * 32 + gl;
+  const int64_t vctas = units / units_per_cta;  // virtual CTAs of the launch
+  const int tiles = gridDim.y;
+  const int64_t d_lo = window.first ? 0 : window_diag(offsets, n, b, window.row0, G, gl, group_mask, group_base);
+  const int64_t d_hi = window_diag(offsets, n, b, window.row1, G, gl, group_mask, group_base);
+  const int64_t path = d_hi - d_lo;
+  __shared__ int64_t s_claim;
+
+  // Virtual CTAs: with `work`, the resident CTAs take them from a counter
+  // (several per CTA, so CTAs that run slower -- the far die, a busier
+  // memory channel -- take fewer and the kernel does not wait on the
+  // slowest of one static wave); without it, virtual CTA = blockIdx.x.
+  for (int64_t claim = blockIdx.x * tiles + blockIdx.y;;) {
+    if (work) {
+      if (threadIdx.x == 0) s_claim = static_cast<int64_t>(atomicAdd(work, 1ull));
+      __syncthreads();
+      claim = s_claim;
+      __syncthreads();
+    }
+    if (claim >= vctas * tiles) break;
+    const int64_t vcta = claim / tiles;
+    const int tile = static_cast<int>(claim % tiles);
+  const int64_t unit = vcta * units_per_cta + unit_in_cta;  // < units by construction
+  const int cv = tile * 32 + gl;
   const bool active = cv < vec_cols;
   const int64_t col = static_cast<int64_t>(cv) * VEC;
 
   // This unit's slice of the merge path.
-  const int64_t d_lo = window.first ? 0 : window_diag(offsets, n, b, window.row0, G, gl, group_mask, group_base);
-  const int64_t d_hi = window_diag(offsets, n, b, window.row1, G, gl, group_mask, group_base);
-  const int64_t path = d_hi - d_lo;
   const int64_t d0 = d_lo + path / units * unit + min(unit, path % units);
   const int64_t d1 = d0 + path / units + (unit < path % units ? 1 : 0);
   const int64_t i0 = path_search(offsets, b, d0, G, gl, group_mask, group_base);
@@ -429,13 +448,16 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   // at its end), written to global memory for the fix-up.
   if (threadIdx.x < G) {
     const int c_lane = threadIdx.x;
-    const int c_cv = blockIdx.y * 32 + c_lane;
-    float *const cta_pieces = pieces + static_cast<int64_t>(blockIdx.x) * 2 * W * d;
+    const int c_cv = tile * 32 + c_lane;
+    float *const cta_pieces = pieces + vcta * 2 * W * d;
     const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
     auto piece = [&](int k, int slot) { return &s_piece[slot][((k << g_shift) + c_lane) * VEC * W]; };
     combine_pieces<T, OP, VEC>(units_per_cta, piece, VEC, s_head, s_tail, s_kind, c_cv < vec_cols, out, d, c_col,
                                cta_pieces + c_col, cta_pieces + W * d + c_col, d,
-                               blockIdx.y == 0 && c_lane == 0 ? &meta[blockIdx.x] : nullptr);
+                               tile == 0 && c_lane == 0 ? &meta[vcta] : nullptr);
+  }
+    if (!work) break;
+    __syncthreads();  // the combine is done with the shared pieces before the next virtual CTA
   }
 }
 
@@ -599,7 +621,7 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
 // its end (TAIL and THROUGH pieces, no HEAD).  Their merged f32 pieces go
 // to the window's edge record instead of out; one extra CTA (blockIdx.x ==
 // units) handles the start and writes the record's header.
-constexpr int kFixupThreads = 256;
+constexpr int kFixupThreads = 512;
 
 // Edge record of one window (floats): a header of kEdgeHeader floats
 // holding int64 {head_seg, head_ends, tail_seg, 0}, then the head piece and
@@ -626,17 +648,26 @@ __device__ __forceinline__ void chain_merge(RowAcc<OP, VEC> &total, const float 
   const int64_t count = hi > lo ? hi - lo : 0;
   const int64_t per = (count + NW - 1) / NW;
   const int64_t a = lo + warp * per, e = a + per < hi ? a + per : hi;
+  // Every CTA of a chain holds a slot-1 piece, so no metadata is read: four
+  // pieces' loads are issued together, then merged in order.
   Acc acc;
   acc.init();
   if (active) {
-    for (int64_t v = a; v < e; v += 4) {
-      int32_t kind[4];
+    int64_t v = a;
+    for (; v + 4 <= e; v += 4) {
+      float buf[4][Acc::kWidth][VEC];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) kind[i] = v + i < e ? meta[v + i].tail_kind : PIECE_NONE;
+      for (int i = 0; i < 4; ++i) {
+        const float *src = pieces + (v + i) * span + Acc::kWidth * d + col;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (kind[i] != PIECE_NONE) acc.merge_piece(pieces + (v + i) * span + Acc::kWidth * d + col, d);
+        for (int k = 0; k < Acc::kWidth; ++k)
+#pragma unroll
+          for (int x = 0; x < VEC; ++x) buf[i][k][x] = __ldcg(src + k * d + x);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc.merge_piece(&buf[i][0][0], VEC);
     }
+    for (; v < e; ++v) acc.merge_piece(pieces + v * span + Acc::kWidth * d + col, d);
   }
   if (active) acc.store_piece(&s_part[warp][0][lane * VEC], 32 * VEC);
   __syncthreads();

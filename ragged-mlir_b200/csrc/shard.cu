@@ -50,15 +50,16 @@ int shard_blocks_per_sm(const void *kernel, int device, int *blocks) {
 }
 
 struct ShardPlan {
-  int64_t ctas, units;
-  int64_t pieces_bytes, meta_bytes;
+  int64_t vctas, grid;
+  int64_t pieces_bytes, meta_bytes, counter;
 };
 
 constexpr int64_t kAlign = 256;
 int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
-// One resident wave of CTAs (per column tile), no more than one unit per 64
-// items of the window's path (bounded by its rows plus all segment ends).
+// Virtual CTAs of the row-balanced kernel (several per resident CTA, taken
+// from a counter), no more than one unit per 64 items of the window's path
+// (bounded by its rows plus all segment ends).
 template <typename T, typename OffT, int OP, int VEC>
 int shard_plan(const Problem &p, const Geometry &g, int64_t rows, ShardPlan *plan) {
   DeviceProps dev;
@@ -68,16 +69,20 @@ int shard_plan(const Problem &p, const Geometry &g, int64_t rows, ShardPlan *pla
   status = shard_blocks_per_sm(reinterpret_cast<const void *>(&rowbal_kernel<T, OffT, OP, VEC>), dev.device, &per_sm);
   if (status) return status;
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
-  int64_t ctas = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
+  int64_t resident = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
+  if (resident < 1) resident = 1;
   const int64_t path = rows + p.b;
   const int64_t wanted = (path + 64 * units_per_cta - 1) / (64 * units_per_cta);
-  if (wanted < ctas) ctas = wanted;
-  if (ctas < 1) ctas = 1;
-  plan->ctas = ctas;
-  plan->units = ctas * units_per_cta;
+  const int64_t per = path / (resident * 16384);  // as the single-GPU plan: up to 8 per CTA
+  int64_t vctas = resident * (per < 1 ? 1 : (per > 8 ? 8 : per));
+  if (vctas > wanted) vctas = wanted;
+  if (vctas < 1) vctas = 1;
+  plan->vctas = vctas;
+  plan->grid = resident < vctas ? resident : vctas;
   const int width = OP == OP_SUM ? 2 : 1;
-  plan->pieces_bytes = align_up(ctas * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
-  plan->meta_bytes = align_up(ctas * static_cast<int64_t>(sizeof(UnitMeta)));
+  plan->pieces_bytes = align_up(vctas * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
+  plan->meta_bytes = align_up(vctas * static_cast<int64_t>(sizeof(UnitMeta)));
+  plan->counter = plan->pieces_bytes + plan->meta_bytes;
   return RG_OK;
 }
 
@@ -94,23 +99,29 @@ int shard_typed(const Problem &p, const Geometry &g, const ShardCall &c, void *w
   int status = shard_plan<T, OffT, OP, VEC>(p, g, c.row1 - c.row0, &plan);
   if (status) return status;
   if (bytes) {
-    *bytes = plan.pieces_bytes + plan.meta_bytes;
+    *bytes = plan.counter + kAlign;
     return RG_OK;
   }
   float *pieces = static_cast<float *>(workspace);
   UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
-  dim3 grid(static_cast<unsigned>(plan.ctas), g.col_tiles, 1);
+  unsigned long long *counter =
+      reinterpret_cast<unsigned long long *>(static_cast<char *>(workspace) + plan.counter);
+  status = check_cuda(cudaMemsetAsync(counter, 0, sizeof *counter, stream), "cudaMemsetAsync");
+  if (status) return status;
+  if (report) report->memsets += 1;
+  const int64_t units = plan.vctas * ((kRowbalThreads / 32) << (5 - g.g_shift));
+  dim3 grid(static_cast<unsigned>(plan.grid), g.col_tiles, 1);
   rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b, p.d,
-      g.g_shift, g.vec_cols, plan.units, pieces, meta, RowWindow{c.row0, c.row1, c.first});
+      g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{c.row0, c.row1, c.first}, counter);
   record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch (shard)");
   if (status) return status;
-  // Every CTA with a TAIL piece, plus one CTA for the window's start and the
-  // edge record's header.
-  dim3 fix_grid(static_cast<unsigned>(plan.ctas + 1), g.col_tiles, 1);
+  // Every virtual CTA with a TAIL piece, plus one CTA for the window's start
+  // and the edge record's header.
+  dim3 fix_grid(static_cast<unsigned>(plan.vctas + 1), g.col_tiles, 1);
   rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols,
-                                                                          plan.ctas, pieces, meta, c.edges);
+                                                                          plan.vctas, pieces, meta, c.edges);
   record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
   return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch (shard)");
 }
