@@ -283,7 +283,7 @@ RANK_MS: list = []  # mean step time of every rank in the last multi-GPU timing
 def ours(args) -> None:
     import torch
     from ragged import ArtifactCache, Compiler, ProgramSpec
-    from ragged.sharding import segment_owners, shard_rows, torch_exchange
+    from ragged.sharding import END_WEIGHT, balanced_split, segment_owners, shard_rows, torch_exchange
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -301,7 +301,8 @@ def ours(args) -> None:
     if world > 1 and w.op == "softmax":
         raise SystemExit("sharded calls compute sum and max; run softmax workloads with --gpus 1")
     offsets_host = w.offsets()
-    rows = shard_rows(w.n, world, rank)
+    splits = balanced_split(offsets_host, world, END_WEIGHT) if world > 1 else None
+    rows = shard_rows(w.n, world, rank, splits)
     values = device_values(torch, w, rows, device)
     offsets = torch.from_numpy(offsets_host).to(device)
     tdtype = values.dtype
@@ -327,7 +328,7 @@ def ours(args) -> None:
     def step():
         if world > 1:
             report_holder["r"] = program.run_sharded(values, offsets, out, total_rows=w.n, world=world, rank=rank,
-                                                     exchange=exchange)
+                                                     exchange=exchange, splits=splits)
         else:
             report_holder["r"] = program.run(values, offsets, out, select=select, max_len=max_len)
 
@@ -358,14 +359,15 @@ def ours(args) -> None:
                          "kernel": "whole call per GPU (all kernels of the schedule; the slowest rank)"},
             "clocks": clocks.summary()}
     if world > 1:
-        line["sharding"] = {"rows_per_rank": [list(shard_rows(w.n, world, r)) for r in range(world)],
+        line["sharding"] = {"rows_per_rank": [list(shard_rows(w.n, world, r, splits)) for r in range(world)],
+                            "split": f"rows + {END_WEIGHT} x segment ends balanced across ranks",
                             "rank_ms": list(RANK_MS),
                             "collective": "NCCL all-gather of edge records",
                             "edge_bytes_per_rank": _native_edge_bytes(w)}
     if not args.no_e2e:
-        owners = segment_owners(offsets_host, world) if w.op != "softmax" else None
+        owners = segment_owners(offsets_host, world, splits) if w.op != "softmax" else None
         line["e2e"] = e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream, dist,
-                              rows, owners, rank, world, exchange)
+                              splits, owners, rank, world, exchange)
     if not args.no_cpu_baseline and rank == 0 and world == 1:
         line["cpu_baseline"] = {k: v for k, v in run_cpu_baseline(w, args.cpu_seconds).items()
                                 if k != "seconds_per_call"}
@@ -391,7 +393,7 @@ def host_memory_available() -> int:
     return 0
 
 
-def e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream, dist=None, rows=None,
+def e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream, dist=None, splits=None,
             owners=None, rank=0, world=1, exchange=None) -> dict:
     """Same metric with inputs in pinned host memory; every step copies this
     rank's rows and the offsets in and the rows of out this rank finishes
@@ -422,7 +424,8 @@ def e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select,
         values.copy_(host_values, non_blocking=True)
         dev_offsets.copy_(host_offsets, non_blocking=True)
         if world > 1:
-            program.run_sharded(values, dev_offsets, out, total_rows=w.n, world=world, rank=rank, exchange=exchange)
+            program.run_sharded(values, dev_offsets, out, total_rows=w.n, world=world, rank=rank, exchange=exchange,
+                                splits=splits)
         else:
             program.run(values, dev_offsets, out, select=select, max_len=max_len)
         host_out.copy_(out[first:last], non_blocking=True)

@@ -139,24 +139,32 @@ const char *rg_kernel_name(int kernel_id);
  * The reference is single-GPU; these entry points are this build's
  * multi-GPU extension of its launcher (runtime/Driver.h:21-54). */
 
-/* Rows [*row0, *row1) of rank `rank` in a row-balanced split of n rows. */
+/* Rows [*row0, *row1) of rank `rank` in the even row split of n rows. */
 int rg_shard_rows(int64_t n, int world, int rank, int64_t *row0, int64_t *row1);
+
+/* A split balanced by work: splits[0..world] (host memory) such that every
+ * rank holds about the same rows + end_weight x segment ends (a segment end
+ * writes an output row; 1.25 balances bf16 D=256 on B200).  offsets is
+ * HOST memory (b + 1 entries).  Pass the split to the calls below; NULL
+ * there means the even row split. */
+int rg_shard_split(const void *offsets, int index_dtype, int64_t b, int world, double end_weight, int64_t *splits);
 
 /* Bytes of one rank's edge record (header + two f32 pieces of D features). */
 int rg_shard_edge_bytes(int op, int64_t d, int64_t *bytes);
 
 /* Scratch bytes rg_run_shard needs (256-byte aligned) on the current device. */
 int rg_shard_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world,
-                             int rank, uint32_t flags, int64_t *bytes);
+                             int rank, const int64_t *splits, uint32_t flags, int64_t *bytes);
 
-/* Reduce rank `rank`'s rows (rg_shard_rows) of a call over n rows and b
- * segments: values holds those rows (the first first), offsets all b + 1
- * entries, out all b rows (only the rows this rank finishes are written),
- * edges this rank's edge record (rg_shard_edge_bytes, 16-byte aligned
- * device memory).  Segments that end at row 0 belong to rank 0. */
+/* Reduce rank `rank`'s rows (splits[rank] to splits[rank + 1], or the even
+ * split when splits is NULL) of a call over n rows and b segments: values
+ * holds those rows (the first first), offsets all b + 1 entries (device),
+ * out all b rows (only the rows this rank finishes are written), edges this
+ * rank's edge record (rg_shard_edge_bytes, 16-byte aligned device memory).
+ * Segments that end at row 0 belong to rank 0. */
 int rg_run_shard(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world, int rank,
-                 const void *values, const void *offsets, void *out, void *edges, void *workspace,
-                 int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report);
+                 const int64_t *splits, const void *values, const void *offsets, void *out, void *edges,
+                 void *workspace, int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report);
 
 /* Finish the segments cut by shard boundaries that this rank owns, from
  * the gathered edge records of ranks 0..world-1 (device memory, rank

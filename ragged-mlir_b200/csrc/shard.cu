@@ -173,16 +173,56 @@ int combine_typed(const Geometry &g, int64_t d, int world, int rank, const float
   return check_cuda(cudaGetLastError(), "shard_combine_kernel launch");
 }
 
-// Op and split checks shared by the shard entry points; the rank's rows.
-int shard_window(int op, int64_t n, int world, int rank, int64_t *row0, int64_t *row1) {
+// Op and split checks shared by the shard entry points; the rank's rows:
+// splits[rank], splits[rank + 1] from the caller's split (host memory,
+// world + 1 nondecreasing entries from 0 to n), or the even row split.
+int shard_window(int op, int64_t n, int world, int rank, const int64_t *splits, int64_t *row0, int64_t *row1) {
   if (op != RG_OP_SUM && op != RG_OP_MAX)
     return fail(RG_ERR_UNSUPPORTED, "sharded calls compute sum and max (softmax is single-GPU in this build)");
   if (n < 0 || world < 1 || rank < 0 || rank >= world)
     return fail(RG_ERR_INVALID_ARGUMENT, "need N >= 0, world >= 1 and 0 <= rank < world");
+  if (splits) {
+    if (splits[0] != 0 || splits[world] != n)
+      return fail(RG_ERR_INVALID_ARGUMENT, "a split must run from row 0 to row N");
+    for (int k = 0; k < world; ++k)
+      if (splits[k] > splits[k + 1]) return fail(RG_ERR_INVALID_ARGUMENT, "split boundaries must not decrease");
+    *row0 = splits[rank];
+    *row1 = splits[rank + 1];
+    return RG_OK;
+  }
   const int64_t q = n / world, rem = n % world;
   *row0 = q * rank + (rank < rem ? rank : rem);
   *row1 = *row0 + q + (rank < rem ? 1 : 0);
   return RG_OK;
+}
+
+// Segment ends at or before row r (host offsets).
+template <typename OffT>
+int64_t ends_at_or_before(const OffT *offsets, int64_t b, int64_t r) {
+  int64_t lo = 0, hi = b;  // first k with offsets[k+1] > r
+  while (lo < hi) {
+    const int64_t mid = lo + (hi - lo) / 2;
+    if (static_cast<int64_t>(offsets[mid + 1]) > r) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+template <typename OffT>
+void balanced_split(const OffT *offsets, int64_t b, int world, double end_weight, int64_t *splits) {
+  const int64_t n = b > 0 ? static_cast<int64_t>(offsets[b]) : 0;
+  const double total = static_cast<double>(n) + end_weight * static_cast<double>(b);
+  splits[0] = 0;
+  for (int k = 1; k < world; ++k) {
+    const double target = total * k / world;
+    int64_t lo = splits[k - 1], hi = n;  // first row r with cost(r) >= target
+    while (lo < hi) {
+      const int64_t mid = lo + (hi - lo) / 2;
+      const double cost = static_cast<double>(mid) + end_weight * static_cast<double>(ends_at_or_before(offsets, b, mid));
+      if (cost >= target) hi = mid; else lo = mid + 1;
+    }
+    splits[k] = lo;
+  }
+  splits[world] = n;
 }
 
 }  // namespace
@@ -198,7 +238,17 @@ int rg_shard_rows(int64_t n, int world, int rank, int64_t *row0, int64_t *row1) 
   if (n < 0 || world < 1 || rank < 0 || rank >= world)
     return fail(RG_ERR_INVALID_ARGUMENT, "need N >= 0, world >= 1 and 0 <= rank < world");
   // Row-balanced split; n / world * r + min(r, n % world) avoids overflow.
-  return shard_window(RG_OP_SUM, n, world, rank, row0, row1);
+  return shard_window(RG_OP_SUM, n, world, rank, nullptr, row0, row1);
+}
+
+int rg_shard_split(const void *offsets, int index_dtype, int64_t b, int world, double end_weight, int64_t *splits) {
+  if (!offsets || !splits) return fail(RG_ERR_INVALID_ARGUMENT, "offsets and splits must not be NULL");
+  if (b < 0 || world < 1) return fail(RG_ERR_INVALID_ARGUMENT, "need B >= 0 and world >= 1");
+  if (!(end_weight >= 0.0)) return fail(RG_ERR_INVALID_ARGUMENT, "end_weight must be nonnegative");
+  if (index_dtype == RG_INDEX_I32) balanced_split(static_cast<const int32_t *>(offsets), b, world, end_weight, splits);
+  else if (index_dtype == RG_INDEX_I64) balanced_split(static_cast<const int64_t *>(offsets), b, world, end_weight, splits);
+  else return fail(RG_ERR_INVALID_ARGUMENT, "offsets dtype must be i32 or i64");
+  return RG_OK;
 }
 
 int rg_shard_edge_bytes(int op, int64_t d, int64_t *bytes) {
@@ -211,10 +261,10 @@ int rg_shard_edge_bytes(int op, int64_t d, int64_t *bytes) {
 }
 
 int rg_shard_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world,
-                             int rank, uint32_t flags, int64_t *bytes) {
+                             int rank, const int64_t *splits, uint32_t flags, int64_t *bytes) {
   if (!bytes) return fail(RG_ERR_INVALID_ARGUMENT, "bytes is NULL");
   int64_t row0 = 0, row1 = 0;
-  int status = shard_window(op, n, world, rank, &row0, &row1);
+  int status = shard_window(op, n, world, rank, splits, &row0, &row1);
   if (status) return status;
   Problem p{op, dtype, index_dtype, d, n, b, nullptr, nullptr, nullptr, -1, flags};
   if ((dtype != RG_DTYPE_F32 && dtype != RG_DTYPE_BF16) || (index_dtype != RG_INDEX_I32 && index_dtype != RG_INDEX_I64) ||
@@ -231,15 +281,15 @@ int rg_shard_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int6
 }
 
 int rg_run_shard(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world, int rank,
-                 const void *values, const void *offsets, void *out, void *edges, void *workspace,
-                 int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report) {
+                 const int64_t *splits, const void *values, const void *offsets, void *out, void *edges,
+                 void *workspace, int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report) {
   if (report) {
     std::memset(report, 0, sizeof *report);
     report->schedule = RG_SCHEDULE_ROWBALANCED;
     report->streams = 1;
   }
   int64_t row0 = 0, row1 = 0;
-  int status = shard_window(op, n, world, rank, &row0, &row1);
+  int status = shard_window(op, n, world, rank, splits, &row0, &row1);
   if (status) return status;
   // The local tensors: values holds the window's rows, out all B rows.
   Problem local{op, dtype, index_dtype, d, row1 - row0, b, values, offsets, out, -1, flags};

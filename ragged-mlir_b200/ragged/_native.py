@@ -29,7 +29,7 @@ MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.
 EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
-            "rg_run", "rg_kernel_name", "rg_shard_rows", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
+            "rg_run", "rg_kernel_name", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
             "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
 
 
@@ -87,9 +87,11 @@ def library(path: Path | None = None):
         lib.rg_shard_rows.restype = i32
         lib.rg_shard_edge_bytes.argtypes = [i32, i64, pi64]
         lib.rg_shard_edge_bytes.restype = i32
-        lib.rg_shard_workspace_bytes.argtypes = [i32, i32, i32, i64, i64, i64, i32, i32, u32, pi64]
+        lib.rg_shard_split.argtypes = [p, i32, i64, i32, ctypes.c_double, pi64]
+        lib.rg_shard_split.restype = i32
+        lib.rg_shard_workspace_bytes.argtypes = [i32, i32, i32, i64, i64, i64, i32, i32, pi64, u32, pi64]
         lib.rg_shard_workspace_bytes.restype = i32
-        lib.rg_run_shard.argtypes = [i32, i32, i32, i64, i64, i64, i32, i32, p, p, p, p, p, i64, u32, p,
+        lib.rg_run_shard.argtypes = [i32, i32, i32, i64, i64, i64, i32, i32, pi64, p, p, p, p, p, i64, u32, p,
                                      ctypes.POINTER(Report)]
         lib.rg_run_shard.restype = i32
         lib.rg_shard_combine.argtypes = [i32, i32, i64, i32, i32, p, p, u32, p]
@@ -166,21 +168,41 @@ def shard_edge_bytes(op: str, d: int) -> int:
     return int(out.value)
 
 
+def _splits_arg(splits):
+    if splits is None:
+        return None
+    array = (ctypes.c_int64 * len(splits))(*[int(x) for x in splits])
+    return ctypes.cast(array, ctypes.POINTER(ctypes.c_int64)), array
+
+
+def shard_split(offsets_host, index: str, world: int, end_weight: float) -> list[int]:
+    """Work-balanced split (world + 1 row boundaries) of host offsets."""
+    import numpy as np
+    offs = np.ascontiguousarray(offsets_host, dtype=np.int32 if index == "i32" else np.int64)
+    out = (ctypes.c_int64 * (world + 1))()
+    raise_for(library().rg_shard_split(offs.ctypes.data, INDEX[index], offs.size - 1, world, float(end_weight),
+                                       ctypes.cast(out, ctypes.POINTER(ctypes.c_int64))), "rg_shard_split")
+    return [int(x) for x in out]
+
+
 def shard_workspace_bytes(op: str, dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int,
-                          flags: int = 0) -> int:
+                          flags: int = 0, splits=None) -> int:
     out = ctypes.c_int64(0)
-    raise_for(library().rg_shard_workspace_bytes(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank, flags,
-                                                 ctypes.byref(out)), "rg_shard_workspace_bytes")
+    arg = _splits_arg(splits)
+    raise_for(library().rg_shard_workspace_bytes(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank,
+                                                 arg[0] if arg else None, flags, ctypes.byref(out)),
+              "rg_shard_workspace_bytes")
     return int(out.value)
 
 
 def run_shard(op: str, dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int, values_ptr: int,
               offsets_ptr: int, out_ptr: int, edges_ptr: int, workspace_ptr: int, workspace_bytes: int, flags: int,
-              stream: int) -> Report:
+              stream: int, splits=None) -> Report:
     report = Report()
-    status = library().rg_run_shard(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank, values_ptr or None,
-                                    offsets_ptr, out_ptr, edges_ptr, workspace_ptr or None, workspace_bytes, flags,
-                                    stream or None, ctypes.byref(report))
+    arg = _splits_arg(splits)
+    status = library().rg_run_shard(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank, arg[0] if arg else None,
+                                    values_ptr or None, offsets_ptr, out_ptr, edges_ptr, workspace_ptr or None,
+                                    workspace_bytes, flags, stream or None, ctypes.byref(report))
     raise_for(status, "rg_run_shard")
     return report
 

@@ -228,12 +228,13 @@ class CompiledProgram:
         return self._report(schedule, selection, started, report, nbytes)
 
     def run_sharded(self, values, offsets, out, *, total_rows: int, world: int, rank: int, exchange,
-                    stream=None) -> ExecutionReport:
+                    stream=None, splits=None) -> ExecutionReport:
         """One rank's part of a row-sharded sum or max (``ragged.sharding``).
 
         ``values`` holds this rank's rows ``sharding.shard_rows(total_rows,
-        world, rank)`` of a call over ``total_rows`` rows, ``offsets`` all B+1
-        entries, ``out`` all B
+        world, rank, splits)`` of a call over ``total_rows`` rows (``splits``:
+        world + 1 row boundaries, e.g. ``sharding.balanced_split``; None: the
+        even row split), ``offsets`` all B+1 entries, ``out`` all B
         output rows (only the rows this rank finishes are written:
         ``sharding.segment_owners``).  ``exchange(edges)`` must return the
         edge records of ranks 0..world-1 concatenated (an all-gather); it is
@@ -244,7 +245,8 @@ class CompiledProgram:
         torch = _torch()
         if not 0 <= rank < world:
             raise ValidationError("need 0 <= rank < world")
-        row0, row1 = _native.shard_rows(total_rows, world, rank)
+        from .sharding import shard_rows
+        row0, row1 = shard_rows(total_rows, world, rank, splits)
         for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
             if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
                 raise RuntimeUnavailable(f"{name} must be a CUDA tensor; no CPU execution fallback exists")
@@ -265,7 +267,7 @@ class CompiledProgram:
             active = stream if stream is not None else torch.cuda.current_stream(values.device)
             spec = self.spec
             nbytes = _native.shard_workspace_bytes(spec.op, spec.dtype, spec.offsets_dtype, d, total_rows, b, world,
-                                                   rank, self._flags)
+                                                   rank, self._flags, splits)
             with torch.cuda.stream(active):
                 scratch = torch.empty((max(nbytes, 1),), dtype=torch.uint8, device=values.device)
                 edges = torch.empty((_native.shard_edge_bytes(spec.op, d) // 4,), dtype=torch.float32,
@@ -273,7 +275,7 @@ class CompiledProgram:
                 report = _native.run_shard(spec.op, spec.dtype, spec.offsets_dtype, d, total_rows, b, world, rank,
                                            values.data_ptr() if values.numel() else 0, offsets.data_ptr(),
                                            out.data_ptr(), edges.data_ptr(), scratch.data_ptr(), nbytes, self._flags,
-                                           active.cuda_stream)
+                                           active.cuda_stream, splits)
                 gathered = exchange(edges)
                 if gathered.numel() != world * edges.numel() or gathered.device != values.device:
                     raise ValidationError("exchange must return every rank's edge record on this device")

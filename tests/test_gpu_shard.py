@@ -19,7 +19,7 @@ from oracle import reference_port as rp
 pytestmark = pytest.mark.gpu
 
 
-def run_world(torch, op, dtype, values, offsets, world):
+def run_world(torch, op, dtype, values, offsets, world, splits=None):
     from ragged import _native
     from ragged.sharding import segment_owners, shard_rows
     d = values.shape[1]
@@ -32,22 +32,23 @@ def run_world(torch, op, dtype, values, offsets, world):
     edges = torch.empty((world, edge_floats), dtype=torch.float32, device="cuda")
     outs = []
     for rank in range(world):
-        row0, row1 = shard_rows(n, world, rank)
-        assert (row0, row1) == _native.shard_rows(n, world, rank)
+        row0, row1 = shard_rows(n, world, rank, splits)
+        if splits is None:
+            assert (row0, row1) == _native.shard_rows(n, world, rank)
         local = dev_values[row0:row1].contiguous()
         out = torch.full((b, d), SENTINEL, dtype=tdtype, device="cuda")
-        ws = _native.shard_workspace_bytes(op, dtype, index, d, n, b, world, rank)
+        ws = _native.shard_workspace_bytes(op, dtype, index, d, n, b, world, rank, 0, splits)
         scratch = torch.empty((max(ws, 1),), dtype=torch.uint8, device="cuda")
         _native.run_shard(op, dtype, index, d, n, b, world, rank, local.data_ptr() if local.numel() else 0,
                           dev_offsets.data_ptr(), out.data_ptr(), edges[rank].data_ptr(), scratch.data_ptr(), ws, 0,
-                          torch.cuda.current_stream().cuda_stream)
+                          torch.cuda.current_stream().cuda_stream, splits)
         outs.append(out)
     gathered = edges.reshape(-1).contiguous()
     for rank in range(world):
         _native.shard_combine(op, dtype, d, world, rank, gathered.data_ptr(), outs[rank].data_ptr(), 0,
                               torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
-    owners = segment_owners(offsets, world)
+    owners = segment_owners(offsets, world, splits)
     host = [o.float().cpu().numpy().astype(np.float64) for o in outs]
     result = np.empty((b, d), dtype=np.float64)
     for rank in range(world):
@@ -118,3 +119,20 @@ def test_sharded_i32_bimodal_and_determinism(cuda):
     again = run_world(cuda, "sum", "bf16", values, offsets, 4)
     np.testing.assert_array_equal(first, again)
     check(first, values, offsets, "sum", "bf16")
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("world", [2, 5, 8])
+def test_sharded_balanced_split(cuda, op, world):
+    """The work-balanced split (rows + weighted segment ends), from the C
+    library's rg_shard_split and its NumPy restatement alike."""
+    from ragged import _native
+    from ragged.sharding import balanced_split
+    lengths = make_lengths("burst", 2000, 80_000, seed=world)
+    lengths[:700] = 1  # many short segments at the start pull the split forward
+    offsets = offsets_of(lengths)
+    splits = balanced_split(offsets, world)
+    assert splits == _native.shard_split(offsets, "i64", world, 1.25)
+    values = prepared(np.random.default_rng(world).normal(size=(int(offsets[-1]), 64)), "bf16")
+    actual = run_world(cuda, op, "bf16", values, offsets, world, splits)
+    check(actual, values, offsets, op, "bf16")

@@ -92,15 +92,16 @@ def combine(op, records, rank, d):
 def _worker(rank, world, port, cases, results):
     import torch
     import torch.distributed as dist
-    from ragged.sharding import shard_rows
+    from ragged.sharding import balanced_split, shard_rows
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         out = []
-        for op, values, offsets in cases:
+        for op, values, offsets, balanced in cases:
             n = int(offsets[-1])
-            row0, row1 = shard_rows(n, world, rank)
+            splits = balanced_split(offsets, world) if balanced else None
+            row0, row1 = shard_rows(n, world, rank, splits)
             finished, record = rank_part(op, values[row0:row1], offsets, row0, row1, rank)
             mine = torch.from_numpy(record)
             gathered = [torch.empty_like(mine) for _ in range(world)]
@@ -134,20 +135,20 @@ def _cases():
         values[10, 1] = np.nan
         cases.append((op, values, offsets))
         cases.append((op, rng.normal(size=(2, 2)), np.array([0, 0, 2, 2], dtype=np.int64)))  # more ranks than rows
-    return cases
+    return [(op, values, offsets, balanced) for op, values, offsets in cases for balanced in (False, True)]
 
 
 @pytest.mark.parametrize("world", [2, 3])
 def test_sharding_protocol_over_gloo(world):
     import torch.multiprocessing as mp
     from oracle import reference_port as rp
-    from ragged.sharding import segment_owners
+    from ragged.sharding import balanced_split, segment_owners
     cases = _cases()
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.start_processes(_worker, args=(world, _free_port(), cases, results), nprocs=world, start_method="spawn")
-    for i, (op, values, offsets) in enumerate(cases):
-        owners = segment_owners(offsets, world)
+    for i, (op, values, offsets, balanced) in enumerate(cases):
+        owners = segment_owners(offsets, world, balanced_split(offsets, world) if balanced else None)
         seen = {}
         for rank in range(world):
             for s, row in results[rank][i].items():
