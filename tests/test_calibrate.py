@@ -1,0 +1,47 @@
+"""Cost-model calibration on CPU: the fit recovers generating coefficients
+and the chosen schedules follow them (as the reference's
+test/python/test_calibrate.py checks its fit)."""
+from __future__ import annotations
+
+import numpy as np
+
+from ragged import calibrate
+from ragged.selection import CostModel, family
+
+
+def synthetic_runs(coefficients, l2_mib=126.0):
+    cases = []
+    for case in calibrate.suite(seed=7, count=90):
+        case = dict(case, max_len=max(1, case["n"] // max(1, case["b"]) * 3))
+        times = {}
+        fam = family(case["op"])
+        for schedule, coef in coefficients[fam].items():
+            terms = calibrate._terms(case, l2_mib)
+            times[schedule] = float(np.dot(coef, terms))
+        cases.append(dict(case, times_us=times))
+    return cases
+
+
+def test_fit_recovers_generating_coefficients():
+    truth = {"reduce": {"classified": [12.0, 0.2, 0.0, 0.05, 0.0, 0.0],
+                        "naive": [6.0, 0.22, 3.0, 0.3, 0.0, 0.0],
+                        "rowbalanced": [10.0, 0.17, 0.0, 0.02, 0.0, 0.0]},
+             "softmax": {"classified": [14.0, 0.4, 0.5, 0.05, 0.0, 0.0],
+                         "naive": [6.0, 0.5, 6.0, 0.3, 0.0, 0.0]}}
+    cases = synthetic_runs(truth)
+    fitted = calibrate.fit_coefficients(cases, 126.0)
+    for fam, schedules in truth.items():
+        for schedule, coef in schedules.items():
+            np.testing.assert_allclose(fitted[fam][schedule], coef, rtol=1e-3, atol=1e-3)
+    model = CostModel(fitted, 0.0, {}, 126.0)
+    hits, total, misses = calibrate.within_share(model, cases, 126.0)
+    assert hits == total, misses
+
+
+def test_suite_is_seeded_and_split():
+    a, b = calibrate.suite(seed=3, count=30), calibrate.suite(seed=3, count=30)
+    assert a == b
+    assert {c["group"] for c in a} == {"train", "heldout"}
+    for distribution in calibrate.DISTRIBUTIONS:
+        lengths = calibrate.lengths_of(distribution, 100, 10_000, np.random.default_rng(1))
+        assert lengths.sum() == 10_000 and (lengths >= 0).all()
