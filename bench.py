@@ -44,6 +44,12 @@ sys.path.insert(0, str(REPO / "ragged-mlir_b200"))
 from ragged import workloads  # noqa: E402
 
 PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+
+# DRAM traffic (ncu dram__bytes_read.sum + dram__bytes_write.sum) over the
+# algorithmic bytes of the dominant kernel, from a capture of a smaller case
+# of the same workload (traffic grows in proportion to the rows): see
+# profiles/rowbal_kernel_c5.md.
+TRAFFIC_RATIO = {"c5": 1.003}
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -353,10 +359,13 @@ def ours(args) -> None:
             "gpu_launches": launches,
             "step_times_ms": [round(t, 4) for t in times],
             "roofline": {"bound": "hbm", "achieved": round(per_rank / (ms / 1e3) / 1e9, 2), "peak": peak,
-                         "unit": "GB/s", "frac": round(per_rank / (ms / 1e3) / 1e9 / peak, 4), "traffic": None,
+                         "unit": "GB/s", "frac": round(per_rank / (ms / 1e3) / 1e9 / peak, 4),
+                         "traffic": (round(TRAFFIC_RATIO[w.name] * per_rank) if w.name in TRAFFIC_RATIO and
+                                     args.scale == 1.0 else None),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s",
-                         "kernel": "whole call per GPU (all kernels of the schedule; the slowest rank)"},
+                         "kernel": "whole call per GPU (all kernels of the schedule; the slowest rank); for c5 the "
+                                   "rowbal_kernel is 99.5% of its device time (ncu launch list)"},
             "clocks": clocks.summary()}
     if world > 1:
         line["sharding"] = {"rows_per_rank": [list(shard_rows(w.n, world, r, splits)) for r in range(world)],
