@@ -17,11 +17,20 @@ namespace rgb {
 
 constexpr int kFoldUnroll = 4;
 
+// A thread's rows are begin + row_lane + k * step for k = 0, 1, ...: a
+// source hands out a cursor at the first one, and the cursor the raw vector
+// of the k-th (one pointer and one stride per loop, no per-row index math).
 template <typename T, int VEC>
 struct GlobalRows {
   using Raw = typename VecIO<T, VEC>::Raw;
   const T *values;
   int64_t d, col;
+  struct Cursor {
+    const T *p;
+    int64_t stride;
+    __device__ __forceinline__ Raw raw(int k) const { return VecIO<T, VEC>::load_raw(p + k * stride); }
+  };
+  __device__ __forceinline__ Cursor at(int64_t r, int64_t step) const { return Cursor{values + r * d + col, step * d}; }
   __device__ __forceinline__ Raw raw(int64_t r) const { return VecIO<T, VEC>::load_raw(values + r * d + col); }
 };
 
@@ -33,10 +42,24 @@ struct SharedRows {
   const char *base;
   int64_t row0;
   int row_bytes, col_bytes;
+  struct Cursor {
+    const char *p;
+    int stride;
+    __device__ __forceinline__ Raw raw(int k) const { return *reinterpret_cast<const Raw *>(p + k * stride); }
+  };
+  __device__ __forceinline__ Cursor at(int64_t r, int64_t step) const {
+    return Cursor{base + static_cast<int>(r - row0) * row_bytes + col_bytes, static_cast<int>(step) * row_bytes};
+  }
   __device__ __forceinline__ Raw raw(int64_t r) const {
     return *reinterpret_cast<const Raw *>(base + static_cast<int>(r - row0) * row_bytes + col_bytes);
   }
 };
+
+// Rows of this thread in [begin, end): begin + row_lane + k * step.
+__device__ __forceinline__ int lane_rows(int64_t begin, int64_t end, int64_t row_lane, int64_t step) {
+  const int64_t first = begin + row_lane;
+  return first < end ? static_cast<int>((end - first + step - 1) / step) : 0;
+}
 
 // Fold rows [begin, end) with stride `step` starting at begin + row_lane:
 // batches of kFoldUnroll rows (loads issued together, one recentring test
@@ -46,19 +69,21 @@ __device__ __forceinline__ void fold_rows(Acc<OP, VEC> &acc, const Src &src, int
                                           int64_t row_lane, int64_t step) {
   constexpr int U = kFoldUnroll;
   using Raw = typename VecIO<T, VEC>::Raw;
-  int64_t r = begin + row_lane;
-  for (; r + (U - 1) * step < end; r += U * step) {
+  const int count = lane_rows(begin, end, row_lane, step);
+  const auto cur = src.at(begin + row_lane, step);
+  int k = 0;
+  for (; k + U <= count; k += U) {
     Raw raw[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
+    for (int u = 0; u < U; ++u) raw[u] = cur.raw(k + u);
     float x[U][VEC];
 #pragma unroll
     for (int u = 0; u < U; ++u) VecIO<T, VEC>::unpack(raw[u], x[u]);
     acc.template fold_batch<U>(x);
   }
-  for (; r < end; r += step) {
+  for (; k < count; ++k) {
     float x[VEC];
-    VecIO<T, VEC>::unpack(src.raw(r), x);
+    VecIO<T, VEC>::unpack(cur.raw(k), x);
     acc.fold(x);
   }
 }
@@ -73,8 +98,11 @@ __device__ __forceinline__ void rows_max(float (&m)[VEC], const Src &src, int64_
   if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
     const __nv_bfloat162 lowest = __floats2bfloat162_rn(-kInf, -kInf);
     __nv_bfloat162 acc[4] = {lowest, lowest, lowest, lowest};
-    for (int64_t r = begin + row_lane; r < end; r += step) {
-      const uint4 raw = src.raw(r);
+    const int count = lane_rows(begin, end, row_lane, step);
+    const auto cur = src.at(begin + row_lane, step);
+#pragma unroll 4
+    for (int k = 0; k < count; ++k) {
+      const uint4 raw = cur.raw(k);
       acc[0] = __hmax2_nan(acc[0], *reinterpret_cast<const __nv_bfloat162 *>(&raw.x));
       acc[1] = __hmax2_nan(acc[1], *reinterpret_cast<const __nv_bfloat162 *>(&raw.y));
       acc[2] = __hmax2_nan(acc[2], *reinterpret_cast<const __nv_bfloat162 *>(&raw.z));
@@ -89,9 +117,12 @@ __device__ __forceinline__ void rows_max(float (&m)[VEC], const Src &src, int64_
   } else {
 #pragma unroll
     for (int v = 0; v < VEC; ++v) m[v] = -kInf;
-    for (int64_t r = begin + row_lane; r < end; r += step) {
+    const int count = lane_rows(begin, end, row_lane, step);
+    const auto cur = src.at(begin + row_lane, step);
+#pragma unroll 4
+    for (int k = 0; k < count; ++k) {
       float x[VEC];
-      VecIO<T, VEC>::unpack(src.raw(r), x);
+      VecIO<T, VEC>::unpack(cur.raw(k), x);
 #pragma unroll
       for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], x[v]);
     }
@@ -130,34 +161,26 @@ __device__ __forceinline__ void staged_stats(Acc<OP_SOFTMAX, VEC> &acc, const Sr
 #pragma unroll
       for (int k = 0; k < P; ++k) s2[k] = add2_rn(s2[k], exp_diff2(pack2(x[2 * k], x[2 * k + 1]), b2[k]));
     };
-    int64_t r = begin + row_lane;
-    for (; r + (U - 1) * step < end; r += U * step) {
+    const int count = lane_rows(begin, end, row_lane, step);
+    const auto cur = src.at(begin + row_lane, step);
+    int k = 0;
+    for (; k + U <= count; k += U) {
       Raw raw[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
+      for (int u = 0; u < U; ++u) raw[u] = cur.raw(k + u);
 #pragma unroll
       for (int u = 0; u < U; ++u) add_row(raw[u]);
     }
-    for (; r < end; r += step) add_row(src.raw(r));
+    for (; k < count; ++k) add_row(cur.raw(k));
 #pragma unroll
     for (int k = 0; k < P; ++k) unpack2(s2[k], s[2 * k], s[2 * k + 1]);
   } else {
-    int64_t r = begin + row_lane;
-    for (; r + (U - 1) * step < end; r += U * step) {
-      Raw raw[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        float x[VEC];
-        VecIO<T, VEC>::unpack(raw[u], x);
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) s[v] = __fadd_rn(s[v], exp_diff(x[v], base[v]));
-      }
-    }
-    for (; r < end; r += step) {
+    const int count = lane_rows(begin, end, row_lane, step);
+    const auto cur = src.at(begin + row_lane, step);
+#pragma unroll 4
+    for (int k = 0; k < count; ++k) {
       float x[VEC];
-      VecIO<T, VEC>::unpack(src.raw(r), x);
+      VecIO<T, VEC>::unpack(cur.raw(k), x);
 #pragma unroll
       for (int v = 0; v < VEC; ++v) s[v] = __fadd_rn(s[v], exp_diff(x[v], base[v]));
     }
@@ -226,24 +249,28 @@ __device__ __forceinline__ void normalize_rows(const Src &src, T *__restrict__ o
                                                const float (&ref)[VEC], const float (&inv)[VEC]) {
   constexpr int U = kFoldUnroll;
   using Raw = typename VecIO<T, VEC>::Raw;
-  int64_t r = begin + row_lane;
-  for (; r + (U - 1) * step < end; r += U * step) {
+  const int count = lane_rows(begin, end, row_lane, step);
+  const auto cur = src.at(begin + row_lane, step);
+  T *const o = out + (begin + row_lane) * d + col;
+  const int64_t ostride = step * d;
+  int k = 0;
+  for (; k + U <= count; k += U) {
     Raw raw[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) raw[u] = src.raw(r + u * step);
+    for (int u = 0; u < U; ++u) raw[u] = cur.raw(k + u);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       float x[VEC], y[VEC];
       VecIO<T, VEC>::unpack(raw[u], x);
       normalize_vec<VEC>(x, y, ref, inv);
-      VecIO<T, VEC>::store(out + (r + u * step) * d + col, y);
+      VecIO<T, VEC>::store(o + (k + u) * ostride, y);
     }
   }
-  for (; r < end; r += step) {
+  for (; k < count; ++k) {
     float x[VEC], y[VEC];
-    VecIO<T, VEC>::unpack(src.raw(r), x);
+    VecIO<T, VEC>::unpack(cur.raw(k), x);
     normalize_vec<VEC>(x, y, ref, inv);
-    VecIO<T, VEC>::store(out + r * d + col, y);
+    VecIO<T, VEC>::store(o + k * ostride, y);
   }
 }
 

@@ -12,13 +12,16 @@
 // consecutive stages for one team.  So every row is read from HBM once by the worker; for softmax the
 // statistics and the normalisation both read shared memory.
 //
-// Consumers classify each segment of a run by length, as the reference's
-// classify kernel does (lib/Conversion/ToGPU.cpp:923-998, thresholds of
-// lib/Transforms/Passes.cpp:17-18): a segment of at most 32 rows goes to one
-// warp (shuffles only), a longer one to a team of 4 warps (shuffles, then a
-// named barrier and a fixed-order merge through shared memory).  Split
-// chunks go to a team too; they leave f32 partials, and the team finishing a
-// segment's last chunk merges them (see classified.cuh).
+// Each stage belongs to one team of 4 consumer warps (the producer rotates
+// the teams), so three stages are reduced at once and a team's barriers
+// never wait on another team.  The team classifies each segment of a run by
+// length, as the reference's classify kernel does (lib/Conversion/
+// ToGPU.cpp:923-998, thresholds of lib/Transforms/Passes.cpp:17-18): a
+// segment of at most 32 rows goes to one of its warps (shuffles only), a
+// longer one to the whole team (shuffles, then a named barrier and a fixed-
+// order merge through shared memory).  A split chunk's stages all go to one
+// team; chunks leave f32 partials, and the team finishing a segment's last
+// chunk merges them (see classified.cuh).
 //
 // Stage protocol: full[s] completes when the producer has written the
 // stage's record and the copy's bytes have landed (arrive.expect_tx +
@@ -39,6 +42,7 @@ constexpr int kPipeThreads = 32 * (kPipeConsumerWarps + 1);
 constexpr int kPipeProducer = kPipeConsumerWarps;  // warp index of the producer
 constexpr int kPipeClaim = 32;                     // segments claimed per atomic
 constexpr int kSmemBudget = 227 * 1024;
+constexpr uint32_t kPieceBytes = 4096;  // bytes per bulk-copy request (a multiple of 16)
 
 template <int OP>
 struct PipeStages {
@@ -82,21 +86,19 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
 // Merge the row groups of a team (kPipeTeamWarps warps), leaving the
 // result for column lane cl in part[tw0 * 32 + cl] where tw0 is the team's
 // first warp; visible to the whole team on return.
+// Every thread merges the team's warp partials itself (in warp order, so
+// all of them hold the same bits): two barriers, no serial merge.
 template <int OP, int VEC>
 __device__ __forceinline__ void team_merge(Acc<OP, VEC> &acc, Acc<OP, VEC> *part, int team, int wit, int q, int cl,
                                            int G) {
   for (int m = 16; m >= G; m >>= 1) acc.shfl_xor_merge(m);
   const int base = team * kPipeTeamWarps;
-  named_sync(1 + team, 32 * kPipeTeamWarps);  // part[] of the team's previous merge has been consumed
+  named_sync(1 + team, 32 * kPipeTeamWarps);  // part[] of the team's previous merge has been read
   if (q == 0) part[(base + wit) * 32 + cl] = acc;
   named_sync(1 + team, 32 * kPipeTeamWarps);
-  if (wit == 0 && q == 0) {
-    Acc<OP, VEC> total = part[base * 32 + cl];
+  acc = part[base * 32 + cl];
 #pragma unroll
-    for (int w = 1; w < kPipeTeamWarps; ++w) total.merge(part[(base + w) * 32 + cl]);
-    part[base * 32 + cl] = total;
-  }
-  named_sync(1 + team, 32 * kPipeTeamWarps);
+  for (int w = 1; w < kPipeTeamWarps; ++w) acc.merge(part[(base + w) * 32 + cl]);
 }
 
 // Fold rows held in shared memory: softmax takes its exact-maximum
@@ -153,16 +155,23 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       ++it;
     };
     // Publish stage s: record written by this warp, then the copy (if any).
+    // The copy is cut into kPieceBytes pieces issued by the warp's lanes in
+    // parallel (one TMA request each), all completing on full[s].
     auto publish = [&](int s, const void *src, uint32_t bytes) {
       __syncwarp();
       if (lane == 0) {
         if (bytes > 0) {
           fence_proxy_async_shared();
           mbar_expect_tx(&full[s], bytes);
-          bulk_copy_g2s(stages + static_cast<int64_t>(s) * L::kStageBytes, src, bytes, &full[s]);
         } else {
           mbar_arrive(&full[s]);
         }
+      }
+      __syncwarp();
+      char *const dst = stages + static_cast<int64_t>(s) * L::kStageBytes;
+      for (uint32_t at = static_cast<uint32_t>(lane) * kPieceBytes; at < bytes; at += 32u * kPieceBytes) {
+        const uint32_t n = bytes - at < kPieceBytes ? bytes - at : kPieceBytes;
+        bulk_copy_g2s(dst + at, static_cast<const char *>(src) + at, n, &full[s]);
       }
     };
     // Runs of consecutive short segments, 32 segments per claim.  Claims are
@@ -173,6 +182,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       o0 = sg < a.b ? static_cast<int64_t>(offsets[sg]) : 0;
       o1 = sg < a.b ? static_cast<int64_t>(offsets[sg + 1]) : 0;
     };
+    int team = 0;  // team of the next stage (runs) or chunk (split)
     unsigned long long pending = 0;
     if (lane == 0) pending = atomicAdd(&a.state->work, static_cast<unsigned long long>(kPipeClaim));
     int64_t base = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
@@ -206,11 +216,13 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         StageRecord &r = rec[s];
         if (lane == 0) {
           r.kind = STAGE_RUN;
+          r.team = team;
           r.count = j - i;
           r.seg = base + i;
           r.r0 = start;
           r.r1 = end;
         }
+        team = team + 1 == kPipeTeams ? 0 : team + 1;
         if (lane >= i && lane < j) r.ends[lane - i] = o1;
         publish(s, values + start * d, static_cast<uint32_t>((end - start) * a.row_bytes));
         i = j;
@@ -224,7 +236,6 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
     // Lane l caches split entry wbase + l (first chunk, segment, rows), so
     // walking consecutive chunks needs no search.
     constexpr int kSplitClaim = 4;
-    int team = 0;
     int64_t wbase = -1, w_first = INT64_MAX, w_seg = 0, w_begin = 0, w_end = 0, w_rows = 1, w_chunks = 0;
     auto load_window = [&](int64_t start) {
       wbase = start;
@@ -318,10 +329,9 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
   bool ok = true;
   Acc<OP, VEC> split_acc;  // this team's chunk in progress (stages of one chunk arrive in order)
   split_acc.init();
-  // Round-robin owners of warp-class segments (warps) and CTA-class segments
-  // (teams), counted over the whole stage sequence, which every consumer
-  // warp walks identically.
-  int small_i = 0, medium_i = 0;
+  // Round-robin owner of the team's warp-class segments, counted over the
+  // team's whole stage sequence (the same in every warp of the team).
+  int small_i = 0;
   for (int64_t it = 0;; ++it) {
     const int s = static_cast<int>(it % S);
     ok &= mbar_wait(&full[s], static_cast<uint32_t>((it / S) & 1));
@@ -329,7 +339,10 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
     const int kind = r.kind;
     if (kind == STAGE_DONE) break;
     const SharedRows<T, VEC> rows{stages + static_cast<int64_t>(s) * L::kStageBytes, r.r0, a.row_bytes, col_bytes};
-    if (kind == STAGE_RUN) {
+    if (kind == STAGE_RUN && r.team == team) {
+      // A whole run belongs to one team: its warp-class segments go to the
+      // team's warps in turn, its CTA-class segments to the whole team, so
+      // a team's barriers never wait on another team's work.
       int64_t begin = r.r0;
       const int count = r.count;
       for (int k = 0; k < count; ++k) {
@@ -337,8 +350,8 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         const int64_t seg = r.seg + k;
         if (end - begin <= kWarpClassMax) {
           // ---- warp class: one warp
-          const bool mine = small_i == warp;
-          small_i = small_i + 1 == NC ? 0 : small_i + 1;
+          const bool mine = small_i == wit;
+          small_i = small_i + 1 == kPipeTeamWarps ? 0 : small_i + 1;
           if (mine) {
             Acc<OP, VEC> acc;
             acc.init();
@@ -357,18 +370,12 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
             }
           }
         } else {
-          const bool ours = medium_i == team;
-          medium_i = medium_i + 1 == kPipeTeams ? 0 : medium_i + 1;
-          if (!ours) {
-            begin = end;
-            continue;
-          }
           // ---- CTA class: one team
           Acc<OP, VEC> acc;
           acc.init();
           if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, team_lane, team_step);
           team_merge<OP, VEC>(acc, part, team, wit, q, cl, G);
-          const Acc<OP, VEC> &fin = part[(team * kPipeTeamWarps) * 32 + cl];
+          const Acc<OP, VEC> &fin = acc;
           if constexpr (OP == OP_SOFTMAX) {
             if (active) {
               float ref[VEC], inv[VEC];
@@ -383,7 +390,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         }
         begin = end;
       }
-    } else if (r.team == team) {
+    } else if (kind == STAGE_SPLIT && r.team == team) {
       // ---- split chunk: one team folds the chunk's stages, publishes an
       // f32 partial, and the team finishing the segment's last chunk merges
       const int64_t c = r.chunk, index = r.index, first = r.first, chunks = r.chunks, seg = r.seg;
@@ -404,8 +411,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       }
       Acc<OP, VEC> acc = split_acc;
       team_merge<OP, VEC>(acc, part, team, wit, q, cl, G);
-      Acc<OP, VEC> *const fin = &part[(team * kPipeTeamWarps) * 32];
-      if (wit == 0 && q == 0 && active) store_partial<OP, VEC>(fin[cl], a.partials + (c * W) * d + col, d);
+      if (wit == 0 && q == 0 && active) store_partial<OP, VEC>(acc, a.partials + (c * W) * d + col, d);
       __threadfence();  // release: the partial before the count
       named_sync(1 + team, 32 * kPipeTeamWarps);
       if (wit == 0 && lane == 0) last_flag[team] = atomicAdd(a.done + index, 1u) == static_cast<unsigned>(chunks - 1);
@@ -436,10 +442,10 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         team_merge<OP, VEC>(m, part, team, wit, q, cl, G);
         if (wit == 0 && q == 0 && active) {
           if constexpr (OP == OP_SOFTMAX) {
-            store_partial<OP, VEC>(fin[cl], a.seg_stats + index * 2 * d + col, d);
+            store_partial<OP, VEC>(m, a.seg_stats + index * 2 * d + col, d);
           } else {
             float y[VEC];
-            fin[cl].result(y);
+            m.result(y);
             VecIO<T, VEC>::store(out + seg * d + col, y);
           }
         }
