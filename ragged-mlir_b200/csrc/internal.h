@@ -52,6 +52,7 @@ enum KernelId : int {
   K_ROWBAL_FIXUP = 6,
   K_SHARD_COMBINE = 7,
   K_ROWBAL_PACKED = 8,
+  K_ROWBAL_NORMALIZE = 9,
 };
 
 // Recording helper for rg_report.

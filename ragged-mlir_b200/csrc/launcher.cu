@@ -189,6 +189,7 @@ const char *rg_kernel_name(int kernel_id) {
     case K_ROWBAL_FIXUP: return "rowbalanced_fixup";
     case K_SHARD_COMBINE: return "shard_combine";
     case K_ROWBAL_PACKED: return "rowbalanced_packed";
+    case K_ROWBAL_NORMALIZE: return "rowbalanced_normalize";
   }
   return "";
 }

@@ -32,9 +32,14 @@ int occupancy(const void *kernel, int device, int threads, int *blocks) {
   return RG_OK;
 }
 
+// Resident CTAs per SM requested from ptxas: 3 for sum and max; the softmax
+// statistics (3 floats per feature) get the registers of 2.
+constexpr int minb_of(int op) { return op == OP_SOFTMAX ? 2 : RowbalTuning::kMinBlocks; }
+
 template <typename T, typename OffT, int OP, int VEC>
 const void *kernel_ptr() {
-  return reinterpret_cast<const void *>(&rowbal_kernel<T, OffT, OP, VEC>);
+  return reinterpret_cast<const void *>(
+      &rowbal_kernel<T, OffT, OP, VEC, RowbalTuning::kUnroll, RowbalTuning::kDoubleBuffer, minb_of(OP)>);
 }
 
 // Narrow rows that pack whole rows into 16-byte packets (2, 4 or 8 bytes a
@@ -46,7 +51,7 @@ bool packs(const Problem &p, const Geometry &g) {
 
 template <typename T, typename OffT, int OP, int VEC>
 const void *packed_ptr() {
-  if constexpr (VEC * sizeof(T) < 16) {
+  if constexpr (VEC * sizeof(T) < 16 && OP != OP_SOFTMAX) {
     return reinterpret_cast<const void *>(&rowbal_packed_kernel<T, OffT, OP, VEC>);
   }
   return nullptr;
@@ -69,6 +74,7 @@ struct Plan {
   int64_t vctas;        // row-balanced kernel: virtual CTAs ...
   int64_t grid;         // ... taken by this many resident CTAs (per column tile)
   int64_t pieces_bytes, meta_bytes, counter;  // workspace: pieces, metadata, claim counter
+  int64_t stats, stats_bytes;                  // softmax statistics
 };
 
 // No more than one unit per 64 path items; the packed kernel runs one
@@ -101,10 +107,14 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
     plan->packed_ctas = ctas < 1 ? 1 : ctas;
   }
   const int64_t slots = plan->vctas > plan->packed_ctas ? plan->vctas : plan->packed_ctas;
-  const int width = p.op == RG_OP_SUM ? 2 : 1;
+  const int width = p.op == RG_OP_MAX ? 1 : 2;
   plan->pieces_bytes = align_up(slots * 2 * width * p.d * static_cast<int64_t>(sizeof(float)));
   plan->meta_bytes = align_up(slots * static_cast<int64_t>(sizeof(UnitMeta)));
   plan->counter = plan->pieces_bytes + plan->meta_bytes;
+  // Softmax: the statistics pass leaves (reference, total) per segment and
+  // feature in [B][2][D] f32 for the normalise pass.
+  plan->stats = plan->counter + kAlign;
+  plan->stats_bytes = p.op == RG_OP_SOFTMAX ? align_up(p.b * 2 * p.d * static_cast<int64_t>(sizeof(float))) : 0;
   return RG_OK;
 }
 
@@ -116,12 +126,12 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC>(), packed, &plan);
   if (status) return status;
   if (bytes) {
-    *bytes = plan.counter + kAlign;
+    *bytes = plan.stats + plan.stats_bytes;
     return RG_OK;
   }
   float *pieces = static_cast<float *>(workspace);
   UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
-  if constexpr (VEC * sizeof(T) < 16) {
+  if constexpr (VEC * sizeof(T) < 16 && OP != OP_SOFTMAX) {
     if (packed && reinterpret_cast<uintptr_t>(p.values) % 16 == 0) {
       const int64_t ctas = plan.packed_ctas;
       dim3 grid(static_cast<unsigned>(ctas), 1, 1);
@@ -144,18 +154,40 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   if (status) return status;
   if (report) report->memsets += 1;
   const int64_t units = plan.vctas * ((kRowbalThreads / 32) << (5 - g.g_shift));
+  // Sum and max write out; the softmax statistics pass writes the statistics buffer.
+  T *const target = OP == OP_SOFTMAX ? reinterpret_cast<T *>(static_cast<char *>(workspace) + plan.stats)
+                                     : static_cast<T *>(p.out);
   dim3 grid(static_cast<unsigned>(plan.grid), g.col_tiles, 1);
-  rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
-      static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
+  rowbal_kernel<T, OffT, OP, VEC, RowbalTuning::kUnroll, RowbalTuning::kDoubleBuffer, minb_of(OP)>
+      <<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
+      static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), target, p.n, p.b,
       p.d, g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{0, p.n, 1}, counter);
   record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch");
-  if (status || plan.vctas < 2) return status;
-  dim3 fix_grid(static_cast<unsigned>(plan.vctas), g.col_tiles, 1);
-  rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(static_cast<T *>(p.out), p.d, g.vec_cols,
-                                                                          plan.vctas, pieces, meta, nullptr);
-  record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
-  return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
+  if (status) return status;
+  if (plan.vctas >= 2) {
+    dim3 fix_grid(static_cast<unsigned>(plan.vctas), g.col_tiles, 1);
+    rowbal_fixup_kernel<T, OP, VEC><<<fix_grid, kFixupThreads, 0, stream>>>(target, p.d, g.vec_cols, plan.vctas,
+                                                                            pieces, meta, nullptr);
+    record_launch(report, K_ROWBAL_FIXUP, fix_grid, kFixupThreads, 0);
+    status = check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
+    if (status) return status;
+  }
+  if constexpr (OP == OP_SOFTMAX) {
+    if (p.n > 0) {
+      const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
+      int64_t ctas = plan.grid;
+      const int64_t wanted = (p.n + 16 * units_per_cta - 1) / (16 * units_per_cta);  // >= 16 rows per unit
+      if (ctas > wanted) ctas = wanted;
+      dim3 ngrid(static_cast<unsigned>(ctas), g.col_tiles, 1);
+      rowbal_normalize_kernel<T, OffT, VEC><<<ngrid, kRowbalThreads, 0, stream>>>(
+          static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out),
+          reinterpret_cast<const float *>(target), p.n, p.b, p.d, g.g_shift, g.vec_cols, ctas * units_per_cta);
+      record_launch(report, K_ROWBAL_NORMALIZE, ngrid, kRowbalThreads, 0);
+      status = check_cuda(cudaGetLastError(), "rowbal_normalize_kernel launch");
+    }
+  }
+  return status;
 }
 
 template <typename T, typename OffT, int OP>
@@ -176,8 +208,9 @@ int run_op(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cudaSt
   switch (p.op) {
     case RG_OP_SUM: return run_vec<T, OffT, OP_SUM>(p, g, ws, bytes, s, r);
     case RG_OP_MAX: return run_vec<T, OffT, OP_MAX>(p, g, ws, bytes, s, r);
+    case RG_OP_SOFTMAX: return run_vec<T, OffT, OP_SOFTMAX>(p, g, ws, bytes, s, r);
   }
-  return fail(RG_ERR_UNSUPPORTED, "the row-balanced schedule computes sum and max only");
+  return fail(RG_ERR_INVALID_ARGUMENT, "unknown op");
 }
 
 template <typename T>
@@ -194,7 +227,6 @@ int dispatch(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cuda
 }  // namespace
 
 int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes) {
-  if (p.op == RG_OP_SOFTMAX) return fail(RG_ERR_UNSUPPORTED, "the row-balanced schedule computes sum and max only");
   if (p.b == 0) {
     *bytes = 0;
     return RG_OK;

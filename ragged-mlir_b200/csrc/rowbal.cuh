@@ -135,6 +135,65 @@ struct RowAcc<OP_MAX, VEC> {
   }
 };
 
+// Softmax statistics pass: per feature the online statistics of
+// common.cuh (lagging reference, compensated mass).  A piece is (reference,
+// total mass); a finished segment's statistics go to the f32 statistics
+// buffer (emit), which the normalise pass reads.
+template <int VEC>
+struct RowAcc<OP_SOFTMAX, VEC> {
+  static constexpr int kWidth = 2;
+  Stats st[VEC];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) st[v] = stats_empty();
+  }
+  __device__ __forceinline__ void fold(const float (&x)[VEC]) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      const float one[1] = {x[v]};
+      stats_fold<1>(st[v], one);
+    }
+  }
+  template <int U>
+  __device__ __forceinline__ void fold_batch(const float (&x)[U][VEC]) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      float col[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) col[u] = x[u][v];
+      stats_fold<U>(st[v], col);
+    }
+  }
+  __device__ __forceinline__ void store_piece(float *piece, int64_t stride) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      piece[v] = st[v].r;
+      piece[stride + v] = kahan_value(st[v].s, st[v].c);
+    }
+  }
+  __device__ __forceinline__ void load_piece(const float *piece, int64_t stride) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) st[v] = Stats{piece[v], piece[stride + v], 0.0f};
+  }
+  __device__ __forceinline__ void merge_piece(const float *piece, int64_t stride) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) stats_merge(st[v], Stats{piece[v], piece[stride + v], 0.0f});
+  }
+};
+
+// A finished segment: sum and max round once to the output dtype; softmax
+// statistics go to the f32 statistics buffer [B][2][D] passed as `out`.
+template <typename T, int OP, int VEC>
+__device__ __forceinline__ void emit(RowAcc<OP, VEC> &acc, T *out, int64_t seg, int64_t d, int64_t col) {
+  if constexpr (OP == OP_SOFTMAX) {
+    acc.store_piece(reinterpret_cast<float *>(out) + seg * 2 * d + col, d);
+  } else {
+    float y[VEC];
+    acc.value(y);
+    VecIO<T, VEC>::store(out + seg * d + col, y);
+  }
+}
+
 template <typename OffT>
 __device__ __forceinline__ int64_t load_offset(const OffT *offsets, int64_t i) {
   return static_cast<int64_t>(__ldg(offsets + i));
@@ -198,11 +257,7 @@ __device__ __forceinline__ void combine_pieces(int count, PieceFn piece, int pst
         here = false;
       }
       if (here) {
-        if (active) {
-          float y[VEC];
-          carry.value(y);
-          VecIO<T, VEC>::store(out + h * d + col, y);
-        }
+        if (active) emit<T, OP, VEC>(carry, out, h, d, col);
       } else {
         if (active) carry.store_piece(head_dst, dstride);
         head_seg = h;
@@ -362,9 +417,7 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
       acc.store_piece(my_head, VEC);
       if (gl == 0) s_head[unit_in_cta] = seg;
     } else if (active) {
-      float y[VEC];
-      acc.value(y);
-      VecIO<T, VEC>::store(out + seg * d + col, y);
+      emit<T, OP, VEC>(acc, out, seg, d, col);
     }
     first = false;
     acc.init();
@@ -390,11 +443,40 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   };
   auto fold_batch = [&](const Raw (&raw)[U], int64_t r) {
     if (r + U <= j1 && next_b >= r + U) {
+      if constexpr (OP == OP_SOFTMAX) {
+        float x[U][VEC];
 #pragma unroll
-      for (int t = 0; t < U; ++t) {
-        float x[VEC];
-        VecIO<T, VEC>::unpack(raw[t], x);
-        acc.fold(x);
+        for (int t = 0; t < U; ++t) VecIO<T, VEC>::unpack(raw[t], x[t]);
+        acc.template fold_batch<U>(x);  // one recentring test per batch and feature
+      } else {
+#pragma unroll
+        for (int t = 0; t < U; ++t) {
+          float x[VEC];
+          VecIO<T, VEC>::unpack(raw[t], x);
+          acc.fold(x);
+        }
+      }
+    } else if constexpr (OP == OP_SOFTMAX) {
+      // A segment boundary inside the batch: fold each segment's rows as a
+      // whole batch with the other rows at -inf (they add no mass and do
+      // not move the reference), so the online statistics take one
+      // recentring test per piece instead of one per row.
+      float x[U][VEC];
+#pragma unroll
+      for (int t = 0; t < U; ++t) VecIO<T, VEC>::unpack(raw[t], x[t]);
+      int t0 = 0;
+      const int tn = j1 - r < U ? static_cast<int>(j1 - r) : U;
+      while (t0 < tn) {
+        while (next_b <= r + t0) finish();  // segments ending before this row (incl. empty ones)
+        const int64_t stop = next_b - r;
+        const int t1 = stop < tn ? static_cast<int>(stop) : tn;
+        float xm[U][VEC];
+#pragma unroll
+        for (int t = 0; t < U; ++t)
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) xm[t][v] = (t >= t0 && t < t1) ? x[t][v] : -kInf;
+        acc.template fold_batch<U>(xm);
+        t0 = t1;
       }
     } else {
 #pragma unroll
@@ -744,11 +826,7 @@ rowbal_fixup_kernel(T *__restrict__ out, int64_t d, int vec_cols, int64_t units,
     return;
   }
   chain_merge<OP, VEC>(total, pieces, meta, d, col, active, u, end, true, s_part);
-  if (warp == 0 && active) {
-    float y[VEC];
-    total.value(y);
-    VecIO<T, VEC>::store(out + seg * d + col, y);
-  }
+  if (warp == 0 && active) emit<T, OP, VEC>(total, out, seg, d, col);
 }
 
 // Finish the segments cut by shard boundaries on the rank that consumed
@@ -788,6 +866,78 @@ shard_combine_kernel(T *__restrict__ out, int64_t d, int vec_cols, int world, in
   float y[VEC];
   total.value(y);
   VecIO<T, VEC>::store(out + seg * d + col, y);
+}
+
+// Softmax normalise pass of the row-balanced schedule: out = e^(x - ref) /
+// total with the statistics the statistics pass left per segment.  Rows are
+// split evenly over the units (every row costs the same); each unit walks
+// its rows from the last to the first, so the rows the statistics pass read
+// last -- the ends of its units' slices -- are re-read while still in L2.
+template <typename T, typename OffT, int VEC, int U = 8>
+__global__ void __launch_bounds__(kRowbalThreads, 3)
+rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
+                        const float *__restrict__ stats, int64_t n, int64_t b, int64_t d, int g_shift, int vec_cols,
+                        int64_t units) {
+  const int lane = threadIdx.x & 31;
+  const int G = 1 << g_shift;
+  const int q = lane >> g_shift, gl = lane & (G - 1);
+  const int group_base = q << g_shift;
+  const unsigned group_mask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << group_base);
+  const int units_per_cta = (kRowbalThreads / 32) << (5 - g_shift);
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * units_per_cta + (threadIdx.x >> 5) * (32 >> g_shift) + q;
+  const int cv = blockIdx.y * 32 + gl;
+  const bool active = cv < vec_cols;
+  const int64_t col = static_cast<int64_t>(cv) * VEC;
+  const int64_t r0 = n / units * unit + min(unit, n % units);
+  const int64_t r1 = r0 + n / units + (unit < n % units ? 1 : 0);
+  if (r1 <= r0) return;  // uniform per unit; no barriers below
+  // Segment of the last row: the first k with offsets[k + 1] > r1 - 1.
+  int64_t seg = ends_upto(offsets, b, r1 - 1, G, gl, group_mask, group_base);
+  int64_t start = load_offset(offsets, seg);
+  float ref[VEC], inv[VEC];
+  auto load_stats = [&]() {
+    const float *st = stats + seg * 2 * d + col;
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      ref[v] = __ldcg(st + v);
+      inv[v] = stats_inverse(__ldcg(st + d + v));
+    }
+  };
+  if (active) load_stats();
+  using Raw = typename VecIO<T, VEC>::Raw;
+  const T *const src = values + col;
+  T *const dst = out + col;
+  auto normalize_row = [&](const Raw &raw, int64_t r) {
+    float x[VEC], y[VEC];
+    VecIO<T, VEC>::unpack(raw, x);
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) y[v] = stats_normalize(x[v], ref[v], inv[v]);
+    VecIO<T, VEC>::store(dst + r * d, y);
+  };
+  int64_t r = r1 - 1;
+  for (; r - (U - 1) >= r0; r -= U) {
+    Raw raw[U];
+#pragma unroll
+    for (int t = 0; t < U; ++t)
+      if (active) raw[t] = VecIO<T, VEC>::load_raw(src + (r - t) * d);
+#pragma unroll
+    for (int t = 0; t < U; ++t) {
+      while (r - t < start) {  // the previous segment (skipping empty ones)
+        --seg;
+        start = load_offset(offsets, seg);
+        if (r - t >= start && active) load_stats();
+      }
+      if (active) normalize_row(raw[t], r - t);
+    }
+  }
+  for (; r >= r0; --r) {
+    while (r < start) {
+      --seg;
+      start = load_offset(offsets, seg);
+      if (r >= start && active) load_stats();
+    }
+    if (active) normalize_row(VecIO<T, VEC>::load_raw(src + r * d), r);
+  }
 }
 
 }  // namespace rgb

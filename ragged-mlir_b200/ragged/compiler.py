@@ -27,7 +27,7 @@ from .model import DIALECT_VERSION, ProgramSpec
 _DIGESTS: dict[tuple, str] = {}
 
 # Schedules libragged_b200 implements, per operation family.
-IMPLEMENTED = {"reduce": ("naive", "classified", "rowbalanced"), "softmax": ("naive", "classified")}
+IMPLEMENTED = {"reduce": ("naive", "classified", "rowbalanced"), "softmax": ("naive", "classified", "rowbalanced")}
 
 
 def schedules_for(spec: ProgramSpec) -> list[str]:

@@ -142,9 +142,15 @@ def test_metamorphic_relations(cuda, op, dtype):
         permuted = run(permuted_values, permuted_offsets)
         expected = (np.concatenate([original[offsets[i]:offsets[i + 1]] for i in permutation])
                     if op == "softmax" else original[permutation])
-        np.testing.assert_array_equal(permuted, expected)
         inserted = run(values, [0, 0, 3, 3, 30, 39, 39])
-        np.testing.assert_array_equal(inserted if op == "softmax" else inserted[1:5], original)
+        if schedule == "rowbalanced" and op == "softmax":
+            # The row-balanced schedule cuts the merge path by position, so a
+            # segment's softmax statistics round differently when it moves.
+            np.testing.assert_allclose(permuted, expected, rtol=2e-6, atol=1e-30)
+            np.testing.assert_allclose(inserted, original, rtol=2e-6, atol=1e-30)
+        else:
+            np.testing.assert_array_equal(permuted, expected)
+            np.testing.assert_array_equal(inserted if op == "softmax" else inserted[1:5], original)
         if op == "softmax":
             shifted = run(values + 5, offsets)
             np.testing.assert_allclose(shifted, original, rtol=2e-5 if dtype == "f32" else 2e-2,
