@@ -148,11 +148,15 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
       return check_cuda(cudaGetLastError(), "rowbal_fixup_kernel launch");
     }
   }
-  unsigned long long *counter =
-      reinterpret_cast<unsigned long long *>(static_cast<char *>(workspace) + plan.counter);
-  status = check_cuda(cudaMemsetAsync(counter, 0, sizeof *counter, stream), "cudaMemsetAsync");
-  if (status) return status;
-  if (report) report->memsets += 1;
+  // Claims only when there are more virtual CTAs than resident ones; one
+  // static wave needs no counter (and no memset).
+  unsigned long long *counter = nullptr;
+  if (plan.vctas > plan.grid) {
+    counter = reinterpret_cast<unsigned long long *>(static_cast<char *>(workspace) + plan.counter);
+    status = check_cuda(cudaMemsetAsync(counter, 0, sizeof *counter, stream), "cudaMemsetAsync");
+    if (status) return status;
+    if (report) report->memsets += 1;
+  }
   const int64_t units = plan.vctas * ((kRowbalThreads / 32) << (5 - g.g_shift));
   // Sum and max write out; the softmax statistics pass writes the statistics buffer.
   T *const target = OP == OP_SOFTMAX ? reinterpret_cast<T *>(static_cast<char *>(workspace) + plan.stats)

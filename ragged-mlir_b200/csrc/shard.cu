@@ -104,11 +104,13 @@ int shard_typed(const Problem &p, const Geometry &g, const ShardCall &c, void *w
   }
   float *pieces = static_cast<float *>(workspace);
   UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
-  unsigned long long *counter =
-      reinterpret_cast<unsigned long long *>(static_cast<char *>(workspace) + plan.counter);
-  status = check_cuda(cudaMemsetAsync(counter, 0, sizeof *counter, stream), "cudaMemsetAsync");
-  if (status) return status;
-  if (report) report->memsets += 1;
+  unsigned long long *counter = nullptr;  // claims only with more virtual CTAs than resident ones
+  if (plan.vctas > plan.grid) {
+    counter = reinterpret_cast<unsigned long long *>(static_cast<char *>(workspace) + plan.counter);
+    status = check_cuda(cudaMemsetAsync(counter, 0, sizeof *counter, stream), "cudaMemsetAsync");
+    if (status) return status;
+    if (report) report->memsets += 1;
+  }
   const int64_t units = plan.vctas * ((kRowbalThreads / 32) << (5 - g.g_shift));
   dim3 grid(static_cast<unsigned>(plan.grid), g.col_tiles, 1);
   rowbal_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
