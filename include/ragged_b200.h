@@ -125,6 +125,18 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
 /* Name of a kernel id reported in rg_report.kernel_ids ("" if unknown). */
 const char *rg_kernel_name(int kernel_id);
 
+/* Checked mode: validate offsets[0..b] on the device (caller's stream)
+ * before any main launch.  status (device memory, 7 x int64) receives, per
+ * condition, the earliest offending index or INT64_MAX: 0 offsets[0] != 0,
+ * 1 offsets[b] != n, 2 an offset < 0, 3 an offset > n, 4 a decreasing pair
+ * (left index), 5 a segment shorter than min_len, 6 longer than max_len
+ * (bounds -1 = none; lengths only of in-range monotone pairs).  The caller
+ * reads status back after the stream completes.  Replaces the reference's
+ * offsets-check-v1 validation kernels (docs/checked-abi.md,
+ * lib/Conversion/ToGPU.cpp:1067-1189). */
+int rg_check_offsets(int index_dtype, int64_t n, int64_t b, const void *offsets, int64_t min_len, int64_t max_len,
+                     int64_t *status, void *stream, rg_report *report);
+
 /* ------------------------------------------------ sharded calls (multi-GPU)
  *
  * One process per GPU.  Rank r of `world` holds rows [row0, row1) of the

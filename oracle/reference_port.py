@@ -12,6 +12,9 @@ import it. It restates, in NumPy float64, the semantics of the reference's
 * ``segment_softmax``   follows ``oracle/reference.py:94-106``
 * ``assert_matches``    follows ``oracle/reference.py:109-174`` (tolerances
   ``TOLERANCES`` of ``oracle/reference.py:14``; sum scale = sum|x|)
+* ``offsets_status``    restates the checked mode's device validation
+  (``lib/Conversion/ToGPU.cpp:1067-1189``, contract pinned by the
+  reference's ``test/gpu/test_checked.py:23-45``)
 
 The reference loops over segments in Python; the restatement below is
 vectorised (``np.add.reduceat``-style over nonempty segments, identities
@@ -58,6 +61,43 @@ def validate_offsets(offsets: np.ndarray, n: int) -> np.ndarray:
     if int(offsets[-1]) != n:
         raise ValueError("offsets[-1] must equal N")
     return offsets
+
+
+CHECK_CONDITIONS = ("first_nonzero", "final_mismatch", "negative", "above_n", "nonmonotone", "below_min_len",
+                    "above_max_len")
+
+
+def offsets_status(offsets, n: int, min_len=None, max_len=None) -> dict[str, int]:
+    """Failed checked-mode conditions -> earliest offending index, in the
+    condition order.  Python integers throughout, so extreme i64 endpoints
+    cannot overflow; a length is formed only for a pair with both endpoints
+    in [0, N] and start <= end (the bounds apply to valid segments only)."""
+    offsets = [int(x) for x in offsets]
+    b = len(offsets) - 1
+    found: dict[str, int] = {}
+
+    def note(condition: str, index: int) -> None:
+        found.setdefault(condition, index)
+
+    if offsets[0] != 0:
+        note("first_nonzero", 0)
+    if offsets[b] != n:
+        note("final_mismatch", b)
+    for i, o in enumerate(offsets):
+        if o < 0:
+            note("negative", i)
+        if o > n:
+            note("above_n", i)
+    for i in range(b):
+        start, end = offsets[i], offsets[i + 1]
+        if end < start:
+            note("nonmonotone", i)
+        if 0 <= start <= end <= n:
+            if min_len is not None and end - start < min_len:
+                note("below_min_len", i)
+            if max_len is not None and end - start > max_len:
+                note("above_max_len", i)
+    return {name: found[name] for name in CHECK_CONDITIONS if name in found}
 
 
 def _inputs(values: np.ndarray, offsets: np.ndarray) -> tuple[np.ndarray, np.ndarray]:

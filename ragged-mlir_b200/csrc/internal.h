@@ -53,6 +53,8 @@ enum KernelId : int {
   K_SHARD_COMBINE = 7,
   K_ROWBAL_PACKED = 8,
   K_ROWBAL_NORMALIZE = 9,
+  K_OFFSETS_INIT = 10,
+  K_OFFSETS_CHECK = 11,
 };
 
 // Recording helper for rg_report.

@@ -190,6 +190,8 @@ const char *rg_kernel_name(int kernel_id) {
     case K_SHARD_COMBINE: return "shard_combine";
     case K_ROWBAL_PACKED: return "rowbalanced_packed";
     case K_ROWBAL_NORMALIZE: return "rowbalanced_normalize";
+    case K_OFFSETS_INIT: return "offsets_init";
+    case K_OFFSETS_CHECK: return "offsets_check";
   }
   return "";
 }

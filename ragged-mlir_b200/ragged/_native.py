@@ -29,7 +29,7 @@ MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.
 EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
-            "rg_run", "rg_kernel_name", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
+            "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
             "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
 
 
@@ -80,6 +80,8 @@ def library(path: Path | None = None):
         lib.rg_run.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, p, i64, i32, i64, u32, p,
                                ctypes.POINTER(Report)]
         lib.rg_run.restype = i32
+        lib.rg_check_offsets.argtypes = [i32, i64, i64, p, i64, i64, p, p, ctypes.POINTER(Report)]
+        lib.rg_check_offsets.restype = i32
         lib.rg_run_noalloc.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, u32, p]
         lib.rg_run_noalloc.restype = i32
         pi64 = ctypes.POINTER(i64)
@@ -211,3 +213,13 @@ def shard_combine(op: str, dtype: str, d: int, world: int, rank: int, gathered_p
                   stream: int) -> None:
     raise_for(library().rg_shard_combine(OPS[op], DTYPES[dtype], d, world, rank, gathered_ptr, out_ptr, flags,
                                          stream or None), "rg_shard_combine")
+
+
+def check_offsets(index: str, n: int, b: int, offsets_ptr: int, min_len: int | None, max_len: int | None,
+                  status_ptr: int, stream: int) -> Report:
+    """Launch the checked-mode offsets validation (status: 7 int64 on the device)."""
+    report = Report()
+    raise_for(library().rg_check_offsets(INDEX[index], n, b, offsets_ptr, -1 if min_len is None else min_len,
+                                         -1 if max_len is None else max_len, status_ptr, stream or None,
+                                         ctypes.byref(report)), "rg_check_offsets")
+    return report

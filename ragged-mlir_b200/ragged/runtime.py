@@ -24,6 +24,7 @@ from .cache import Artifact
 from .errors import CacheMismatch, RuntimeUnavailable, ValidationError
 from .model import ExecutionReport, ProgramSpec, runs_on
 from .selection import default_model
+from .validation import CONDITIONS, STATUS_BYTES, raise_for_status
 
 I64_MAX = 2**63 - 1
 # Segment-length class bounds of the classified schedule (warp <= 32 rows,
@@ -113,7 +114,7 @@ class CompiledProgram:
     def close(self) -> None:
         """Nothing to unload: kernels live in the shared library."""
 
-    def _validate_tensors(self, values, offsets, out, torch) -> tuple[int, int]:
+    def _validate_tensors(self, values, offsets, out, torch, checked: bool = False) -> tuple[int, int]:
         for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
             if not isinstance(tensor, torch.Tensor):
                 raise ValidationError(f"{name} must be a torch.Tensor")
@@ -144,7 +145,7 @@ class CompiledProgram:
                                               f"{vector} features at a time (compile with vectorize=False for "
                                               "unaligned views)")
         n, b = values.shape[0], offsets.numel() - 1
-        if b == 0 and n != 0:
+        if b == 0 and n != 0 and not checked:  # checked mode reports it from the device (final_mismatch)
             raise ValidationError("B=0 requires N=0; values cannot exist without segments")
         if self.spec.offsets_dtype == "i32" and n > 2**31 - 1:
             raise ValidationError("N exceeds the i32 offsets range")
@@ -182,9 +183,6 @@ class CompiledProgram:
             raise ValidationError("max_len must be None or a nonnegative int")
         if mode not in ("validated", "checked"):
             raise ValidationError("mode must be validated or checked")
-        if mode == "checked":
-            raise RuntimeUnavailable("checked execution (device offsets validation) is not implemented by "
-                                     "libragged_b200; use validated mode with valid offsets")
         if (mask is not None) != self.spec.mask:
             raise ValidationError("mask presence must match the compiled specialization")
         if debug_buffers is not None:
@@ -192,13 +190,14 @@ class CompiledProgram:
         if select != "auto" and select not in self.schedules:
             raise ValidationError(f"select={select} is not a schedule of this program ({', '.join(self.schedules)})")
         torch = _torch()
-        n, b = self._validate_tensors(values, offsets, out, torch)
+        checked = mode == "checked"
+        n, b = self._validate_tensors(values, offsets, out, torch, checked)
         started = time.perf_counter()
         if select == "auto":
             schedule, selection = self.choose(n, b, max_len, device_l2_mib(values))
         else:
             schedule, selection = select, {"forced": True}
-        if b == 0:
+        if b == 0 and not checked:
             return self._report(schedule, selection, started, None, 0)
         with torch.cuda.device(values.device):
             ordinal = values.device.index
@@ -211,6 +210,9 @@ class CompiledProgram:
             active = stream if stream is not None else torch.cuda.current_stream(values.device)
             if not isinstance(active, torch.cuda.Stream) or active.device != values.device:
                 raise ValidationError("stream must be a torch.cuda.Stream on the values device")
+            validation = self._check_offsets(values, offsets, n, b, active, torch) if checked else None
+            if b == 0:
+                return self._report(schedule, selection, started, None, 0, validation)
             nbytes = self.workspace_bytes(n, b, schedule, max_len)
             scratch, base = None, 0
             if nbytes:
@@ -225,7 +227,26 @@ class CompiledProgram:
             report = _native.run(self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b,
                                  values.data_ptr(), offsets.data_ptr(), out.data_ptr(), base, nbytes, schedule,
                                  max_len, self._flags, active.cuda_stream)
-        return self._report(schedule, selection, started, report, nbytes)
+        return self._report(schedule, selection, started, report, nbytes, validation)
+
+    def _check_offsets(self, values, offsets, n, b, active, torch):
+        """Checked mode (reference python/ragged/runtime.py:506-533): validate
+        the offsets on the device, on the execution stream, before any main
+        kernel or scratch allocation; copy the 56-byte status to pinned host
+        memory, wait on that stream only and raise ValidationError on failure.
+        The length bounds are the spec's hints (None: unchecked)."""
+        started = time.perf_counter()
+        with torch.cuda.stream(active):
+            status = torch.empty((len(CONDITIONS),), dtype=torch.int64, device=values.device)
+            host = torch.empty((len(CONDITIONS),), dtype=torch.int64, device="cpu", pin_memory=True)
+            for tensor in (values, offsets, status):
+                tensor.record_stream(active)
+            report = _native.check_offsets(self.spec.offsets_dtype, n, b, offsets.data_ptr(), self.spec.hints.min_len,
+                                           self.spec.hints.max_len, status.data_ptr(), active.cuda_stream)
+            host.copy_(status, non_blocking=True)
+        active.synchronize()
+        raise_for_status(host.tolist(), b=b)
+        return report, (time.perf_counter() - started) * 1000
 
     def run_sharded(self, values, offsets, out, *, total_rows: int, world: int, rank: int, exchange,
                     stream=None, splits=None) -> ExecutionReport:
@@ -285,20 +306,29 @@ class CompiledProgram:
                               started, report, nbytes)
         return result
 
-    def _report(self, schedule, selection, started, report, nbytes) -> ExecutionReport:
+    def _report(self, schedule, selection, started, report, nbytes, validation=None) -> ExecutionReport:
+        validation, validation_ms = validation if validation is not None else (None, None)
         thresholds = THRESHOLDS if schedule == "classified" else ()
-        if report is None:
-            names, grids, vec, tile, streams = (), (), 1, None, 1
-        else:
-            count = report.num_launches
-            names = tuple(_native.kernel_name(report.kernel_ids[i]) for i in range(count))
-            grids = tuple(tuple(int(x) for x in report.grid[i]) for i in range(count))
+        names, grids, vec, tile, streams = (), (), 1, None, 1
+        for part in (validation, report):
+            if part is None:
+                continue
+            count = part.num_launches
+            names += tuple(_native.kernel_name(part.kernel_ids[i]) for i in range(count))
+            grids += tuple(tuple(int(x) for x in part.grid[i]) for i in range(count))
+        if report is not None:
             vec, tile, streams = int(report.d_vector), int(report.d_tile), int(report.streams)
             if schedule == "classified" and report.thresholds[1] > 0:
                 thresholds = (int(report.thresholds[0]), int(report.thresholds[1]))
         classes = ("cta",) if schedule == "naive" else (("warp", "cta", "split") if schedule == "classified"
                                                         else ("rows",))
-        return ExecutionReport(classes, thresholds, grids, nbytes, self._digest,
-                               None, "validated", names, (time.perf_counter() - started) * 1000,
-                               cache_hit=self.cache_hit, optimizations={"requested": self.spec.optimizations.to_dict()},
+        if report is None:
+            classes = ()
+        checked_bytes = STATUS_BYTES if validation is not None else 0
+        return ExecutionReport(classes, thresholds, grids, nbytes + checked_bytes, self._digest, None,
+                               "checked" if validation is not None else "validated", names,
+                               (time.perf_counter() - started) * 1000, cache_hit=self.cache_hit,
+                               validation_workspace_bytes=checked_bytes,
+                               validation_host_ms=validation_ms if validation is not None else None,
+                               optimizations={"requested": self.spec.optimizations.to_dict()},
                                d_tile=tile, d_vector=vec, streams=streams, selected=schedule, selection=selection)
