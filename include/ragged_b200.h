@@ -59,6 +59,12 @@ enum rg_schedule {
 
 /* rg_run flags */
 #define RG_FLAG_NO_VECTORIZE 1u /* one feature per thread (reference Optimizations(vectorize=False)) */
+/* Softmax only: out IS values (same pointer, N rows), the reference's
+ * ProgramSpec(alias="inplace") (python/ragged/model.py:119-122,
+ * docs/classified-abi.md:208-214).  Every schedule finishes a segment's
+ * statistics reads before it writes any of the segment's rows, and writes
+ * each element only after its last read. */
+#define RG_FLAG_IN_PLACE 2u
 
 #define RG_MAX_LAUNCHES 8
 
@@ -121,6 +127,22 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
            const void *values, const void *offsets, void *out, void *workspace,
            int64_t workspace_bytes, int schedule, int64_t max_len, uint32_t flags,
            void *stream, rg_report *report);
+
+/* Pointwise input transform (the reference's ProgramSpec scale / mask,
+ * docs/mask-abi.md; python/ragged/runtime.py:346-356 for the mask rules):
+ * every value becomes x = f32(values) * scale (scale != 1) + mask (f32
+ * [N][D], softmax only; NULL = none), two f32 roundings, and `op` runs on x
+ * with `schedule`.  The transformed values are materialised in `workspace`
+ * (the reference's route with pointwise fusion off, lib/Conversion/
+ * ToGPU.cpp:41-60, 604-618); results round once to `dtype`.  The mask may
+ * alias values but not out or offsets.  Workspace from
+ * rg_pointwise_workspace_bytes; otherwise as rg_run. */
+int rg_pointwise_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
+                                 int schedule, int64_t max_len, uint32_t flags, int64_t *bytes);
+int rg_run_pointwise(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
+                     const void *values, const void *offsets, const float *mask, float scale, void *out,
+                     void *workspace, int64_t workspace_bytes, int schedule, int64_t max_len, uint32_t flags,
+                     void *stream, rg_report *report);
 
 /* Name of a kernel id reported in rg_report.kernel_ids ("" if unknown). */
 const char *rg_kernel_name(int kernel_id);

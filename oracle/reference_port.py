@@ -12,6 +12,8 @@ import it. It restates, in NumPy float64, the semantics of the reference's
 * ``segment_softmax``   follows ``oracle/reference.py:94-106``
 * ``assert_matches``    follows ``oracle/reference.py:109-174`` (tolerances
   ``TOLERANCES`` of ``oracle/reference.py:14``; sum scale = sum|x|)
+* ``masked_logits``     follows ``oracle/masked.py:13-25`` (x * scale, then
+  + mask, each rounded to f32; the softmax oracle then runs on the result)
 * ``offsets_status``    restates the checked mode's device validation
   (``lib/Conversion/ToGPU.cpp:1067-1189``, contract pinned by the
   reference's ``test/gpu/test_checked.py:23-45``)
@@ -61,6 +63,28 @@ def validate_offsets(offsets: np.ndarray, n: int) -> np.ndarray:
     if int(offsets[-1]) != n:
         raise ValueError("offsets[-1] must equal N")
     return offsets
+
+
+def masked_logits(values, mask=None, *, scale=1.0) -> np.ndarray:
+    """The transformed input of a scale / mask call: f32(values) * f32(scale)
+    (skipped for scale 1) and then + mask, each an f32 rounding, no fused
+    multiply-add; IEEE rules for non-finite values (+inf + -inf = NaN)."""
+    values = np.asarray(values)
+    if values.ndim != 2 or values.dtype.kind != "f":
+        raise ValueError("values must be a floating-point [N, D] array")
+    if mask is not None:
+        mask = np.asarray(mask)
+        if mask.shape != values.shape or mask.dtype != np.float32:
+            raise ValueError("mask must be f32 with exactly the values shape")
+    if isinstance(scale, (bool, np.bool_)) or not np.isfinite(scale):
+        raise ValueError("scale must be a finite f32 value")
+    with np.errstate(over="ignore", invalid="ignore"):
+        x = values.astype(np.float32)
+        if scale != 1.0:
+            x = np.multiply(x, np.float32(scale), dtype=np.float32)
+        if mask is not None:
+            x = np.add(x, mask, dtype=np.float32)
+    return x
 
 
 CHECK_CONDITIONS = ("first_nonzero", "final_mismatch", "negative", "above_n", "nonmonotone", "below_min_len",
@@ -270,7 +294,9 @@ def check_strict(actual: np.ndarray, values: np.ndarray, offsets: np.ndarray, *,
                  reference: np.ndarray | None = None) -> dict[str, float]:
     """This build's stricter contract, on top of the reference's.
 
-    * max: bit-exact values (signed zero excepted), same NaN / +-inf masks;
+    * max: bit-exact values in the output dtype (the round-to-nearest-even
+      of the maximum: the maximum itself unless a scale made it
+      unrepresentable), signed zero excepted, same NaN / +-inf masks;
     * f32 sum:     |a - ref| <= 1e-5 * sum|x|   (cancellation-safe scale);
     * f32 softmax: |a - ref| <= 1e-5 * |ref| + FLT_MIN;
     * bf16 output: |a - RNE(ref)| <= 1 bf16 ulp of RNE(ref) (+ for sum
@@ -284,7 +310,11 @@ def check_strict(actual: np.ndarray, values: np.ndarray, offsets: np.ndarray, *,
     _compare_nonfinite(actual, expected)
     finite = np.isfinite(expected)
     if operation == "max":
-        exact = np.where(finite, actual == expected, True)
+        with np.errstate(over="ignore", invalid="ignore"):
+            rounded = expected.astype(np.float32)
+            if input_dtype == "bf16":
+                rounded = quantize_bf16(rounded)
+        exact = np.where(finite, actual == rounded.astype(np.float64), True)
         if not np.all(exact):
             raise AssertionError(f"max is not bit-exact at {int(np.sum(~exact))} positions")
         return {"max_abs_error": 0.0}

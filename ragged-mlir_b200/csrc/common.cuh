@@ -138,13 +138,11 @@ struct Stats {
 
 __device__ __forceinline__ Stats stats_empty() { return Stats{-kInf, 0.0f, 0.0f}; }
 
-// Fold `count` values x[0..count) (count is a compile-time bound; entries
-// beyond the valid ones must be -inf) into st.
-template <int COUNT>
-__device__ __forceinline__ void stats_fold(Stats &st, const float (&x)[COUNT]) {
-  float bm = x[0];
-#pragma unroll
-  for (int i = 1; i < COUNT; ++i) bm = max_nan(bm, x[i]);
+// Move the reference for a batch whose maximum is bm (the first step of
+// stats_fold).  Afterwards the batch's terms are e^(x - st.r), unless st.r
+// is -inf (no mass: every value so far is -inf) or not finite (the column
+// is NaN already).
+__device__ __forceinline__ void stats_recenter(Stats &st, float bm) {
   const float m = max_nan(st.r, bm);
   const bool empty = st.r == -kInf;
   const bool unordered = (st.r != st.r) || (bm != bm);
@@ -164,7 +162,19 @@ __device__ __forceinline__ void stats_fold(Stats &st, const float (&x)[COUNT]) {
       st.c = 0.0f;
     }
   }
-  if (st.r == -kInf || !is_finite(st.r)) return;  // no mass yet, or the column is already NaN
+}
+
+__device__ __forceinline__ bool stats_has_mass(const Stats &st) { return st.r != -kInf && is_finite(st.r); }
+
+// Fold `count` values x[0..count) (count is a compile-time bound; entries
+// beyond the valid ones must be -inf) into st.
+template <int COUNT>
+__device__ __forceinline__ void stats_fold(Stats &st, const float (&x)[COUNT]) {
+  float bm = x[0];
+#pragma unroll
+  for (int i = 1; i < COUNT; ++i) bm = max_nan(bm, x[i]);
+  stats_recenter(st, bm);
+  if (!stats_has_mass(st)) return;  // no mass yet, or the column is already NaN
   float p = exp_diff(x[0], st.r);
 #pragma unroll
   for (int i = 1; i < COUNT; ++i) p = __fadd_rn(p, exp_diff(x[i], st.r));

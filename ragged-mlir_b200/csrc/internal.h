@@ -55,6 +55,8 @@ enum KernelId : int {
   K_ROWBAL_NORMALIZE = 9,
   K_OFFSETS_INIT = 10,
   K_OFFSETS_CHECK = 11,
+  K_POINTWISE_LOGITS = 12,
+  K_POINTWISE_CAST = 13,
 };
 
 // Recording helper for rg_report.
@@ -65,6 +67,7 @@ int fail(int status, const std::string &message);
 int check_cuda(cudaError_t err, const char *what);
 
 int elem_bytes(int dtype);
+bool aligned(const void *p, int bytes);
 Geometry make_geometry(const Problem &p);
 int device_props(DeviceProps *props);  // current device
 int validate(const Problem &p);           // argument checks of rg_run
@@ -76,5 +79,10 @@ int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
 int launch_rowbal(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
 int classified_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
 int launch_classified(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
+
+// Any schedule: its scratch bytes, and its launch for a validated problem.
+int workspace_for(const Problem &p, const Geometry &g, int schedule, int64_t *bytes);
+int run_schedule(const Problem &p, const Geometry &g, int schedule, void *workspace, cudaStream_t stream,
+                 rg_report *report);
 
 }  // namespace rgb

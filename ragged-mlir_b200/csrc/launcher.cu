@@ -45,7 +45,7 @@ void record_launch(rg_report *report, int kernel_id, dim3 grid, int block, int s
 
 int elem_bytes(int dtype) { return dtype == RG_DTYPE_F32 ? 4 : 2; }
 
-static bool aligned(const void *p, int bytes) {
+bool aligned(const void *p, int bytes) {
   return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(bytes)) == 0;
 }
 
@@ -113,12 +113,17 @@ int validate(const Problem &p) {
   if (!p.offsets) return fail(RG_ERR_INVALID_ARGUMENT, "offsets pointer is NULL");
   if (p.n > 0 && !p.values) return fail(RG_ERR_INVALID_ARGUMENT, "values pointer is NULL");
   if (rows_out > 0 && !p.out) return fail(RG_ERR_INVALID_ARGUMENT, "out pointer is NULL");
-  // out must be disjoint from values and offsets.
+  // out must be disjoint from values (or, in place, be values) and from offsets.
   const uintptr_t ob = reinterpret_cast<uintptr_t>(p.out), oe = ob + rows_out * p.d * esize;
   const uintptr_t vb = reinterpret_cast<uintptr_t>(p.values), ve = vb + p.n * p.d * esize;
   const uintptr_t fb = reinterpret_cast<uintptr_t>(p.offsets),
                   fe = fb + (p.b + 1) * (p.index_dtype == RG_INDEX_I32 ? 4 : 8);
-  if (rows_out > 0 && p.n > 0 && ob < ve && vb < oe) return fail(RG_ERR_INVALID_ARGUMENT, "out overlaps values");
+  if (p.flags & RG_FLAG_IN_PLACE) {
+    if (p.op != RG_OP_SOFTMAX) return fail(RG_ERR_INVALID_ARGUMENT, "in-place output is only defined for softmax");
+    if (p.n > 0 && p.out != p.values) return fail(RG_ERR_INVALID_ARGUMENT, "in place, out must be values");
+  } else if (rows_out > 0 && p.n > 0 && ob < ve && vb < oe) {
+    return fail(RG_ERR_INVALID_ARGUMENT, "out overlaps values");
+  }
   if (rows_out > 0 && ob < fe && fb < oe) return fail(RG_ERR_INVALID_ARGUMENT, "out overlaps offsets");
   if (!aligned(p.offsets, p.index_dtype == RG_INDEX_I32 ? 4 : 8))
     return fail(RG_ERR_INVALID_ARGUMENT, "offsets must be aligned to their element size");
@@ -147,12 +152,23 @@ int check_device(DeviceProps *props) {
 }
 
 // Scratch bytes of `schedule` for this problem (status on failure).
-static int workspace_for(const Problem &p, const Geometry &g, int schedule, int64_t *bytes) {
+int workspace_for(const Problem &p, const Geometry &g, int schedule, int64_t *bytes) {
   *bytes = 0;
   switch (schedule) {
     case RG_SCHEDULE_NAIVE: return RG_OK;
     case RG_SCHEDULE_CLASSIFIED: return classified_workspace(p, g, bytes);
     case RG_SCHEDULE_ROWBALANCED: return rowbal_workspace(p, g, bytes);
+  }
+  return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
+}
+
+// Launch `schedule` for a validated problem (workspace sized by workspace_for).
+int run_schedule(const Problem &p, const Geometry &g, int schedule, void *workspace, cudaStream_t s,
+                 rg_report *report) {
+  switch (schedule) {
+    case RG_SCHEDULE_NAIVE: return launch_naive(p, g, s, report);
+    case RG_SCHEDULE_CLASSIFIED: return launch_classified(p, g, workspace, s, report);
+    case RG_SCHEDULE_ROWBALANCED: return launch_rowbal(p, g, workspace, s, report);
   }
   return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
 }
@@ -192,6 +208,8 @@ const char *rg_kernel_name(int kernel_id) {
     case K_ROWBAL_NORMALIZE: return "rowbalanced_normalize";
     case K_OFFSETS_INIT: return "offsets_init";
     case K_OFFSETS_CHECK: return "offsets_check";
+    case K_POINTWISE_LOGITS: return "pointwise_logits";
+    case K_POINTWISE_CAST: return "pointwise_cast";
   }
   return "";
 }
@@ -261,13 +279,8 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, 
     if (!workspace || workspace_bytes < need) return fail(RG_ERR_WORKSPACE, "workspace missing or too small");
     if (!aligned(workspace, 256)) return fail(RG_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (schedule) {
-    case RG_SCHEDULE_NAIVE: return launch_naive(p, g, s, report);
-    case RG_SCHEDULE_CLASSIFIED: return launch_classified(p, g, workspace, s, report);
-    case RG_SCHEDULE_ROWBALANCED: return launch_rowbal(p, g, workspace, s, report);
-  }
-  return fail(RG_ERR_UNSUPPORTED, "schedule not available in this build");
+  return run_schedule(p, g, schedule, workspace, static_cast<cudaStream_t>(stream), report);
 }
+
 
 }  // extern "C"

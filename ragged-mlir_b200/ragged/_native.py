@@ -25,11 +25,12 @@ INDEX = {"i32": 0, "i64": 1}
 SCHEDULES = {"classified": 0, "naive": 1, "rowbalanced": 2}
 SCHEDULE_NAMES = {value: key for key, value in SCHEDULES.items()}
 FLAG_NO_VECTORIZE = 1
+FLAG_IN_PLACE = 2
 MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.
 EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
-            "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
+            "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_pointwise_workspace_bytes", "rg_run_pointwise", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
             "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
 
 
@@ -82,6 +83,12 @@ def library(path: Path | None = None):
         lib.rg_run.restype = i32
         lib.rg_check_offsets.argtypes = [i32, i64, i64, p, i64, i64, p, p, ctypes.POINTER(Report)]
         lib.rg_check_offsets.restype = i32
+        lib.rg_pointwise_workspace_bytes.argtypes = [i32, i32, i32, i64, i64, i64, i32, i64, u32,
+                                                     ctypes.POINTER(i64)]
+        lib.rg_pointwise_workspace_bytes.restype = i32
+        lib.rg_run_pointwise.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, ctypes.c_float, p, p, i64, i32, i64,
+                                         u32, p, ctypes.POINTER(Report)]
+        lib.rg_run_pointwise.restype = i32
         lib.rg_run_noalloc.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, u32, p]
         lib.rg_run_noalloc.restype = i32
         pi64 = ctypes.POINTER(i64)
@@ -152,6 +159,29 @@ def run(op: str, dtype: str, index: str, d: int, n: int, b: int, values_ptr: int
                               workspace_ptr or None, workspace_bytes, SCHEDULES[schedule],
                               -1 if max_len is None else max_len, flags, stream or None, ctypes.byref(report))
     raise_for(status, "rg_run")
+    return report
+
+
+def pointwise_workspace_bytes(op: str, dtype: str, index: str, d: int, n: int, b: int, schedule: str,
+                              max_len: int | None, flags: int) -> int:
+    """Scratch of a scale / mask call: the f32 logits, results and schedule."""
+    out = ctypes.c_int64(0)
+    raise_for(library().rg_pointwise_workspace_bytes(OPS[op], DTYPES[dtype], INDEX[index], d, n, b,
+                                                     SCHEDULES[schedule], -1 if max_len is None else max_len, flags,
+                                                     ctypes.byref(out)), "rg_pointwise_workspace_bytes")
+    return out.value
+
+
+def run_pointwise(op: str, dtype: str, index: str, d: int, n: int, b: int, values_ptr: int, offsets_ptr: int,
+                  mask_ptr: int, scale: float, out_ptr: int, workspace_ptr: int, workspace_bytes: int, schedule: str,
+                  max_len: int | None, flags: int, stream: int) -> Report:
+    """One call with the input transform x * scale (+ mask for softmax)."""
+    report = Report()
+    status = library().rg_run_pointwise(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, values_ptr, offsets_ptr,
+                                        mask_ptr or None, float(scale), out_ptr, workspace_ptr or None,
+                                        workspace_bytes, SCHEDULES[schedule], -1 if max_len is None else max_len,
+                                        flags, stream or None, ctypes.byref(report))
+    raise_for(status, "rg_run_pointwise")
     return report
 
 

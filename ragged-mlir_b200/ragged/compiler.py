@@ -71,12 +71,6 @@ class Compiler:
     @staticmethod
     def _check_supported(spec: ProgramSpec) -> None:
         unsupported = []
-        if spec.mask:
-            unsupported.append("additive mask")
-        if spec.alias != "none":
-            unsupported.append("in-place softmax")
-        if spec.scale != 1.0:
-            unsupported.append("scale")
         if spec.debug_visits:
             unsupported.append("debug_visits")
         if unsupported:

@@ -2,11 +2,11 @@
 
 Mirrors the reference's python/ragged/model.py (ProgramSpec 129-212, Hints
 114-127, ExecutionReport 256-293) with the B200 target: the only chip is
-``sm_100a`` (compute capability 10.0) and its per-CTA limits.  Fields that
-select reference features outside this build's hot path (additive ``mask``,
-``alias="inplace"``, ``scale`` other than 1, ``debug_visits``) are validated
+``sm_100a`` (compute capability 10.0) and its per-CTA limits.  ``mask``
+and ``scale`` take the materialised input transform (rg_run_pointwise),
+``alias="inplace"`` the in-place softmax flag; ``debug_visits`` is validated
 as in the reference and rejected by ``Compiler.compile`` with a
-``CompilationError`` naming the feature.
+``CompilationError``.
 """
 from __future__ import annotations
 

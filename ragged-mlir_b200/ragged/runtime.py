@@ -85,7 +85,10 @@ class CompiledProgram:
         self._workspace: dict[tuple, int] = {}
         tile, vec = spec.optimizations.geometry(spec.feature_dim, spec.dtype)
         self._span = tile * vec
-        self._flags = 0 if spec.optimizations.vectorize else _native.FLAG_NO_VECTORIZE
+        self._flags = (0 if spec.optimizations.vectorize else _native.FLAG_NO_VECTORIZE) | (
+            _native.FLAG_IN_PLACE if spec.alias == "inplace" else 0)
+        # Scale or mask: the transformed input is materialised (rg_run_pointwise).
+        self._pointwise = spec.mask or float(spec.scale) != 1.0
 
     @property
     def selects(self) -> bool:
@@ -114,8 +117,10 @@ class CompiledProgram:
     def close(self) -> None:
         """Nothing to unload: kernels live in the shared library."""
 
-    def _validate_tensors(self, values, offsets, out, torch, checked: bool = False) -> tuple[int, int]:
-        for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
+    def _validate_tensors(self, values, offsets, out, torch, checked: bool = False, mask=None) -> tuple[int, int]:
+        tensors = (("values", values), ("offsets", offsets), ("out", out)) + ((("mask", mask),) if mask is not None
+                                                                               else ())
+        for name, tensor in tensors:
             if not isinstance(tensor, torch.Tensor):
                 raise ValidationError(f"{name} must be a torch.Tensor")
             if not tensor.is_cuda:
@@ -152,10 +157,25 @@ class CompiledProgram:
         expected = (n if self.spec.op == "softmax" else b, self.spec.feature_dim)
         if tuple(out.shape) != expected:
             raise ValidationError(f"out shape must be {expected}")
+        if mask is not None:  # reference runtime.py:346-356; the mask may alias values (read only)
+            if mask.dtype != torch.float32 or tuple(mask.shape) != tuple(values.shape):
+                raise ValidationError("mask must have f32 dtype and exactly values shape [N,D]; "
+                                      "broadcasting is unsupported")
+            if mask.device != values.device:
+                raise ValidationError("mask must use the values CUDA device")
+            if mask.numel() and mask.data_ptr() % 4:
+                raise ValidationError("mask must be 4-byte aligned")
+            if _overlaps(mask, out) or _overlaps(mask, offsets):
+                raise ValidationError("mask must not overlap out or offsets")
         if _overlaps(offsets, values) or _overlaps(offsets, out):
             raise ValidationError("offsets must not alias values or out")
+        # In place (runtime.py:358-364 of the reference): out must BE values.
+        exact = values.data_ptr() == out.data_ptr() and tuple(values.shape) == tuple(out.shape)
         if _overlaps(values, out):
-            raise ValidationError("out aliases values without a compiler-proven safe in-place schedule")
+            if not exact or self.spec.alias != "inplace":
+                raise ValidationError("out aliases values without a compiler-proven safe in-place schedule")
+        elif self.spec.alias == "inplace" and not (exact and values.numel() == 0):
+            raise ValidationError("in-place specialization requires out and values to be the same buffer")
         return n, b
 
     def workspace_bytes(self, n: int, b: int, schedule: str, max_len: int | None = None) -> int:
@@ -164,7 +184,8 @@ class CompiledProgram:
         if nbytes is None:
             if len(self._workspace) >= 256:
                 self._workspace.clear()
-            nbytes = self._workspace[key] = _native.workspace_bytes(
+            size = _native.pointwise_workspace_bytes if self._pointwise else _native.workspace_bytes
+            nbytes = self._workspace[key] = size(
                 self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b, schedule, max_len,
                 self._flags)
         return nbytes
@@ -191,7 +212,7 @@ class CompiledProgram:
             raise ValidationError(f"select={select} is not a schedule of this program ({', '.join(self.schedules)})")
         torch = _torch()
         checked = mode == "checked"
-        n, b = self._validate_tensors(values, offsets, out, torch, checked)
+        n, b = self._validate_tensors(values, offsets, out, torch, checked, mask)
         started = time.perf_counter()
         if select == "auto":
             schedule, selection = self.choose(n, b, max_len, device_l2_mib(values))
@@ -222,11 +243,18 @@ class CompiledProgram:
                     scratch = torch.empty((nbytes,), dtype=torch.uint8, device=values.device)
                 base = scratch.data_ptr()
             if stream is not None:
-                for tensor in (values, offsets, out):
+                for tensor in (values, offsets, out) + ((mask,) if mask is not None else ()):
                     tensor.record_stream(active)
-            report = _native.run(self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b,
-                                 values.data_ptr(), offsets.data_ptr(), out.data_ptr(), base, nbytes, schedule,
-                                 max_len, self._flags, active.cuda_stream)
+            if self._pointwise:
+                report = _native.run_pointwise(
+                    self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim, n, b,
+                    values.data_ptr(), offsets.data_ptr(), mask.data_ptr() if mask is not None else 0,
+                    float(self.spec.scale), out.data_ptr(), base, nbytes, schedule, max_len, self._flags,
+                    active.cuda_stream)
+            else:
+                report = _native.run(self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim,
+                                     n, b, values.data_ptr(), offsets.data_ptr(), out.data_ptr(), base, nbytes,
+                                     schedule, max_len, self._flags, active.cuda_stream)
         return self._report(schedule, selection, started, report, nbytes, validation)
 
     def _check_offsets(self, values, offsets, n, b, active, torch):
@@ -263,6 +291,8 @@ class CompiledProgram:
         no host synchronisation of its own."""
         if self.spec.op not in ("sum", "max"):
             raise RuntimeUnavailable("sharded calls compute sum and max in this build")
+        if self._pointwise:
+            raise RuntimeUnavailable("sharded calls take no scale (the input transform is single-GPU only)")
         torch = _torch()
         if not 0 <= rank < world:
             raise ValidationError("need 0 <= rank < world")
@@ -331,4 +361,5 @@ class CompiledProgram:
                                validation_workspace_bytes=checked_bytes,
                                validation_host_ms=validation_ms if validation is not None else None,
                                optimizations={"requested": self.spec.optimizations.to_dict()},
+                               pointwise_materialized=self._pointwise,
                                d_tile=tile, d_vector=vec, streams=streams, selected=schedule, selection=selection)

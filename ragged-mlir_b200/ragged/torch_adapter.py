@@ -72,6 +72,22 @@ def _fake_validate(values, offsets, torch) -> None:
         raise ValidationError("values and offsets must use the same device")
 
 
+def _fake_validate_mask(values, mask, torch) -> None:
+    """The additive mask contract (docs/mask-abi.md of the reference): a
+    dense, contiguous f32 tensor of exactly the values shape on the values'
+    device, without autograd."""
+    if mask.dtype != torch.float32:
+        raise ValidationError("mask must be f32")
+    if mask.ndim != 2 or tuple(mask.shape) != tuple(values.shape):
+        raise ValidationError("mask must have exactly values shape [N,D]; broadcasting is unsupported")
+    if not mask.is_contiguous():
+        raise ValidationError("mask must be contiguous")
+    if mask.device != values.device:
+        raise ValidationError("mask must use the values device")
+    if mask.requires_grad:
+        raise ValidationError("autograd is outside the supported forward-only contract")
+
+
 def register_torch_ops() -> dict[str, Any]:
     with _lock:
         if _operators:
@@ -102,6 +118,8 @@ def register_torch_ops() -> dict[str, Any]:
         def softmax_fake(values, offsets, program, mode="validated", mask=None):
             _check_mode(mode)
             _fake_validate(values, offsets, torch)
+            if mask is not None:
+                _fake_validate_mask(values, mask, torch)
             return values.new_empty(values.shape)
 
         _operators.update(segment_reduce=reduce_op, segment_softmax=softmax_op)

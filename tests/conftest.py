@@ -26,6 +26,21 @@ def pytest_configure(config):
 
 
 @pytest.fixture(scope="session")
+def masked_golden():
+    """name -> dict(values, mask, offsets, logits, softmax, dtype, scale) from
+    the reference's oracle/masked.py (tests/golden/make_masked_golden.py)."""
+    import json
+    path = REPO / "tests" / "golden" / "masked.npz"
+    data = np.load(path)
+    cases = {}
+    for case in json.loads(path.with_suffix(".json").read_text())["cases"]:
+        name = case["name"]
+        cases[name] = {key: data[f"{name}__{key}"] for key in ("values", "mask", "offsets", "logits", "softmax")}
+        cases[name].update(dtype=case["dtype"], scale=case["scale"])
+    return cases
+
+
+@pytest.fixture(scope="session")
 def golden():
     """name -> dict(values, offsets, sum, max, softmax, dtype)."""
     import json

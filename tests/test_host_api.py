@@ -66,10 +66,17 @@ def test_compile_cache_hit_and_adaptive(tmp_path, native_library):
 
 def test_unsupported_features_fail_to_compile(tmp_path, native_library):
     cache = ArtifactCache(tmp_path)
+    with pytest.raises(CompilationError, match="not implemented"):
+        Compiler().compile(ProgramSpec("sum", debug_visits=True), cache)
+
+
+def test_mask_scale_and_inplace_specialisations_compile(tmp_path, native_library):
+    cache = ArtifactCache(tmp_path)
     for spec in (ProgramSpec("softmax", mask=True), ProgramSpec("softmax", alias="inplace"),
-                 ProgramSpec("sum", scale=2.0), ProgramSpec("sum", debug_visits=True)):
-        with pytest.raises(CompilationError, match="not implemented"):
-            Compiler().compile(spec, cache)
+                 ProgramSpec("softmax", mask=True, scale=0.5, alias="inplace"), ProgramSpec("sum", scale=2.0),
+                 ProgramSpec("max", "bf16", 8, scale=-1.5)):
+        program = Compiler().compile(spec, cache)
+        assert program.spec == spec
 
 
 def test_cache_rejects_tampering_and_limits(tmp_path, native_library):

@@ -160,3 +160,24 @@ def test_oracle_imports_neither_product_nor_torch():
             else:
                 continue
             assert all(name.split(".")[0] not in {"ragged", "torch", "triton"} for name in names), source
+
+
+def test_masked_logits_match_the_reference_fixtures(masked_golden):
+    """The scale / mask restatement against the reference's own
+    oracle/masked.py outputs (bitwise, NaN positions included)."""
+    for name, case in masked_golden.items():
+        logits = rp.masked_logits(case["values"], case["mask"], scale=case["scale"])
+        np.testing.assert_array_equal(logits, case["logits"], err_msg=name)
+        with np.errstate(all="ignore"):
+            softmax = rp.segment_softmax(logits, case["offsets"])
+        np.testing.assert_allclose(softmax, case["softmax"], rtol=1e-12, atol=0, equal_nan=True, err_msg=name)
+
+
+def test_masked_logits_rejects_bad_contracts():
+    values = np.zeros((3, 2), dtype=np.float32)
+    with pytest.raises(ValueError):
+        rp.masked_logits(values, np.zeros((3, 2), dtype=np.float64))
+    with pytest.raises(ValueError):
+        rp.masked_logits(values, np.zeros((1, 2), dtype=np.float32))
+    with pytest.raises(ValueError):
+        rp.masked_logits(values, None, scale=float("inf"))

@@ -155,3 +155,55 @@ def test_in_place_specialisation_cannot_back_a_functional_op():
                               artifact=SimpleNamespace(key=SimpleNamespace(digest="inplace")))
     with pytest.raises(ValidationError, match="out-of-place"):
         torch_adapter.register_program(program)
+
+
+@pytest.mark.parametrize("problem", ["bf16", "rank", "broadcast", "noncontiguous", "device", "grad"])
+def test_mask_fake_rejects_unsupported_tensor_contract(ops, problem):
+    from ragged import ValidationError
+    values = torch.empty((6, 4), dtype=torch.bfloat16, device="meta")
+    offsets = torch.empty((3,), dtype=torch.int64, device="meta")
+    mask = torch.empty((6, 4), device="meta")
+    if problem == "bf16":
+        mask = mask.to(torch.bfloat16)
+    elif problem == "rank":
+        mask = torch.empty((24,), device="meta")
+    elif problem == "broadcast":
+        mask = torch.empty((1, 4), device="meta")
+    elif problem == "noncontiguous":
+        mask = torch.empty((4, 6), device="meta").t()
+    elif problem == "device":
+        mask = torch.empty((6, 4))
+    else:
+        mask.requires_grad_()
+    with pytest.raises((ValidationError, RuntimeError)):
+        ops["segment_softmax"](values, offsets, "shape-only-no-program", "validated", mask)
+
+
+def test_masked_softmax_fullgraph_keeps_the_mask_operand(ops):
+    class Operation(torch.nn.Module):
+        def forward(self, values, offsets, mask):
+            return ops["segment_softmax"](values, offsets, "shape-only-no-program", "checked", mask)
+
+    args = (torch.empty((6, 4), dtype=torch.bfloat16, device="meta"), torch.empty((3,), dtype=torch.int64, device="meta"),
+            torch.empty((6, 4), device="meta"))
+    output, graph = _capture(Operation(), *args)
+    assert output.shape == (6, 4) and output.dtype == torch.bfloat16
+    nodes = [node for node in graph.graph.nodes if "ragged_mlir.segment_softmax" in str(node.target)]
+    assert len(nodes) == 1 and isinstance(nodes[0].args[-1], torch.fx.Node)
+
+
+def test_njt_mask_routes_the_dense_mask(monkeypatch):
+    from ragged import ProgramSpec, ValidationError
+    from ragged import torch_adapter
+    calls = []
+    program = SimpleNamespace(spec=ProgramSpec("softmax", feature_dim=4, mask=True),
+                              artifact=SimpleNamespace(key=SimpleNamespace(digest="njt-mask-routing")),
+                              run=lambda values, offsets, out, **kwargs: calls.append(kwargs))
+    monkeypatch.setattr(torch_adapter, "_programs", {})
+    values, offsets, mask = torch.empty((6, 4)), torch.tensor([0, 2, 6]), torch.empty((6, 4))
+    out = torch_adapter.njt_softmax(torch.nested.nested_tensor_from_jagged(values, offsets), program=program,
+                                    mode="checked", mask=mask)
+    assert out.values().shape == values.shape and out.offsets().data_ptr() == offsets.data_ptr()
+    assert len(calls) == 1 and calls[0]["mask"] is mask and calls[0]["mode"] == "checked"
+    with pytest.raises(ValidationError, match="mask presence"):
+        torch_adapter.bind(program)(values, offsets)
