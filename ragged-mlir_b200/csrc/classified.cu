@@ -201,7 +201,8 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
       status = blocks_per_sm(norm, dev.device, kClsThreads, 0, &per_sm);
       if (status) return status;
       int64_t nctas = static_cast<int64_t>(per_sm) * dev.sm_count;
-      if (nctas > l.chunks * g.col_tiles) nctas = l.chunks * g.col_tiles;
+      const int64_t warps_needed = l.chunks * g.col_tiles;  // one warp per chunk and column tile
+      if (nctas > (warps_needed + kClsWarps - 1) / kClsWarps) nctas = (warps_needed + kClsWarps - 1) / kClsWarps;
       if (nctas < 1) nctas = 1;
       dim3 ngrid(static_cast<unsigned>(nctas), 1, 1);
       split_normalize_kernel<T, OffT, VEC><<<ngrid, kClsThreads, 0, stream>>>(

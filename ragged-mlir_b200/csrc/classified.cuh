@@ -58,7 +58,7 @@ struct ClsState {
   unsigned long long cta_count;    // CTA-class segments
   unsigned long long split_packed; // (chunks << 28) | split segments
   unsigned long long work;         // next work item of the worker
-  unsigned long long norm_work;    // next work item of the split normaliser
+  unsigned long long norm_work;    // unused (kept for the state layout)
   unsigned long long error;        // nonzero: a bounded wait gave up
   unsigned long long split_work;   // next split chunk of the pipelined worker
   unsigned long long pad;
@@ -364,36 +364,52 @@ cls_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets
   }
 }
 
-// Softmax rows of split segments, normalised with the merged statistics.
-// Chunks are taken in reverse order: the worker read the last chunks most
-// recently, so they are still in L2.
+// Softmax: normalise the rows of split segments with their merged
+// statistics.  One warp per item (a chunk and column tile), items spread
+// statically over the warps in reverse chunk order, so the chunks the
+// worker read last are re-read first, from L2.  A warp finds its chunk's
+// split entry with a 32-ary search of split_base (three steps for 32K
+// split segments) and keeps 8 rows per lane group in flight.
 template <typename T, typename OffT, int VEC>
 __global__ void __launch_bounds__(kClsThreads, 2)
 split_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
                        ClsArgs a) {
-  constexpr int NW = kClsWarps;
-  __shared__ int64_t item_slot[2];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int U = 8;
+  using Raw = typename VecIO<T, VEC>::Raw;
+  const int lane = threadIdx.x & 31;
   const int G = 1 << a.g_shift;
   const int q = lane >> a.g_shift, cl = lane & (G - 1);
-  const int64_t cta_step = static_cast<int64_t>(NW) << (5 - a.g_shift);
-  const int64_t cta_lane = static_cast<int64_t>(warp) * (32 >> a.g_shift) + q;
+  const int upw = 32 >> a.g_shift;
   const unsigned long long packed = __ldcg(&a.state->split_packed);
   const int64_t n_split = static_cast<int64_t>(packed & kSplitCountMask);
   const int64_t n_chunks = static_cast<int64_t>(packed >> kSplitCountBits);
-  const int64_t total = n_chunks * a.col_tiles;
-  for (int parity = 0;; parity ^= 1) {
-    if (threadIdx.x == 0) item_slot[parity] = static_cast<int64_t>(atomicAdd(&a.state->norm_work, 1ull));
-    __syncthreads();
-    const int64_t w = item_slot[parity];
-    if (w >= total) break;
+  const int64_t items = n_chunks * a.col_tiles;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < items;
+       w += warps) {
     const int tile = static_cast<int>(w % a.col_tiles);
     const int64_t c = n_chunks - 1 - w / a.col_tiles;
+    // Last split entry i with split_base[i] <= c (32-ary search).
+    int64_t lo = 0, hi = n_split - 1;
+    while (lo < hi) {
+      const int64_t step = (hi - lo + 31) / 32;
+      const int64_t probe = lo + (lane + 1) * step;
+      const bool le = probe <= hi && __ldcg(a.split_base + probe) <= c;
+      const unsigned m = __ballot_sync(0xffffffffu, le);
+      const int k = m ? 32 - __clz(m) : 0;  // probes lo + 1..k * step are <= c
+      const int64_t cut = lo + static_cast<int64_t>(k + 1) * step - 1;
+      hi = k < 32 && cut < hi ? cut : hi;
+      lo = lo + static_cast<int64_t>(k) * step;
+    }
+    const int64_t index = lo;
+    const int64_t seg = __ldcg(a.split_seg + index), first = __ldcg(a.split_base + index);
+    const int64_t begin = static_cast<int64_t>(offsets[seg]), end = static_cast<int64_t>(offsets[seg + 1]);
+    const int64_t cr = chunk_rows_of(end - begin, a.item_rows);
+    const int64_t r0 = begin + (c - first) * cr;
+    const int64_t r1 = r0 + cr < end ? r0 + cr : end;
     const int cv = tile * 32 + cl;
     if (cv >= a.vec_cols) continue;
     const int64_t col = static_cast<int64_t>(cv) * VEC;
-    int64_t index, seg, r0, r1, first, count;
-    locate_chunk(c, a.item_rows, a.split_base, a.split_seg, n_split, offsets, index, seg, r0, r1, first, count);
     float ref[VEC], inv[VEC];
     const float *st = a.seg_stats + index * 2 * a.d + col;
 #pragma unroll
@@ -401,8 +417,26 @@ split_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ of
       ref[v] = __ldcg(st + v);
       inv[v] = stats_inverse(__ldcg(st + a.d + v));
     }
-    const GlobalRows<T, VEC> rows{values, a.d, col};
-    normalize_rows<T, VEC>(rows, out, a.d, col, r0, r1, cta_lane, cta_step, ref, inv);
+    const int64_t step = upw;
+    int64_t r = r0 + q;
+    for (; r + (U - 1) * step < r1; r += U * step) {
+      Raw raw[U];
+#pragma unroll
+      for (int t = 0; t < U; ++t) raw[t] = VecIO<T, VEC>::load_raw(values + (r + t * step) * a.d + col);
+#pragma unroll
+      for (int t = 0; t < U; ++t) {
+        float x[VEC], y[VEC];
+        VecIO<T, VEC>::unpack(raw[t], x);
+        normalize_vec<VEC>(x, y, ref, inv);
+        VecIO<T, VEC>::store(out + (r + t * step) * a.d + col, y);
+      }
+    }
+    for (; r < r1; r += step) {
+      float x[VEC], y[VEC];
+      VecIO<T, VEC>::unpack(VecIO<T, VEC>::load_raw(values + r * a.d + col), x);
+      normalize_vec<VEC>(x, y, ref, inv);
+      VecIO<T, VEC>::store(out + r * a.d + col, y);
+    }
   }
 }
 

@@ -55,10 +55,12 @@ struct SharedRows {
   }
 };
 
-// Rows of this thread in [begin, end): begin + row_lane + k * step.
+// Rows of this thread in [begin, end): begin + row_lane + k * step.  Every
+// step here is a power of two (lanes per row and warps per team or CTA
+// are), so the count is a shift.
 __device__ __forceinline__ int lane_rows(int64_t begin, int64_t end, int64_t row_lane, int64_t step) {
   const int64_t first = begin + row_lane;
-  return first < end ? static_cast<int>((end - first + step - 1) / step) : 0;
+  return first < end ? static_cast<int>((end - first + step - 1) >> (__ffsll(step) - 1)) : 0;
 }
 
 // Fold rows [begin, end) with stride `step` starting at begin + row_lane:

@@ -14,14 +14,15 @@
 //
 // Each stage belongs to one team of 4 consumer warps (the producer rotates
 // the teams), so three stages are reduced at once and a team's barriers
-// never wait on another team.  The team classifies each segment of a run by
-// length, as the reference's classify kernel does (lib/Conversion/
-// ToGPU.cpp:923-998, thresholds of lib/Transforms/Passes.cpp:17-18): a
-// segment of at most 32 rows goes to one of its warps (shuffles only), a
-// longer one to the whole team (shuffles, then a named barrier and a fixed-
-// order merge through shared memory).  A split chunk's stages all go to one
-// team; chunks leave f32 partials, and the team finishing a segment's last
-// chunk merges them (see classified.cuh).
+// never wait on another team.  Every segment of a run goes to ONE warp of
+// the team (shuffles only, no barrier): the warps take contiguous groups of
+// the run's segments with about equal rows.  (The reference splits its
+// non-split segments at 32 rows between warp and CTA workers, lib/
+// Conversion/ToGPU.cpp:923-998; here a warp-per-segment run measured 1.3x
+// faster on B200 than a 4-warp merge for the segments of 33 to item_rows
+// rows.)  A split chunk's stages all go to one team, whose warps split the
+// rows and merge through a named barrier; chunks leave f32 partials, and
+// the team finishing a segment's last chunk merges them (see classified.cuh).
 //
 // Stage protocol: full[s] completes when the producer has written the
 // stage's record and the copy's bytes have landed (arrive.expect_tx +
@@ -329,9 +330,6 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
   bool ok = true;
   Acc<OP, VEC> split_acc;  // this team's chunk in progress (stages of one chunk arrive in order)
   split_acc.init();
-  // Round-robin owner of the team's warp-class segments, counted over the
-  // team's whole stage sequence (the same in every warp of the team).
-  int small_i = 0;
   for (int64_t it = 0;; ++it) {
     const int s = static_cast<int>(it % S);
     ok &= mbar_wait(&full[s], static_cast<uint32_t>((it / S) & 1));
@@ -340,51 +338,31 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
     if (kind == STAGE_DONE) break;
     const SharedRows<T, VEC> rows{stages + static_cast<int64_t>(s) * L::kStageBytes, r.r0, a.row_bytes, col_bytes};
     if (kind == STAGE_RUN && r.team == team) {
-      // A whole run belongs to one team: its warp-class segments go to the
-      // team's warps in turn, its CTA-class segments to the whole team, so
-      // a team's barriers never wait on another team's work.
-      int64_t begin = r.r0;
+      // A whole run belongs to one team, and each of its segments to one
+      // warp of the team: no team barrier.  Segment k goes to the warp whose
+      // quarter of the run's rows holds the segment's middle row, so the
+      // warps get contiguous groups of segments with about equal rows.
+      const int64_t r0 = r.r0, span = r.r1 - r.r0;
+      int64_t begin = r0;
       const int count = r.count;
       for (int k = 0; k < count; ++k) {
         const int64_t end = r.ends[k];
         const int64_t seg = r.seg + k;
-        if (end - begin <= kWarpClassMax) {
-          // ---- warp class: one warp
-          const bool mine = small_i == wit;
-          small_i = small_i + 1 == kPipeTeamWarps ? 0 : small_i + 1;
-          if (mine) {
-            Acc<OP, VEC> acc;
-            acc.init();
-            if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, q, warp_step);
-            warp_merge<OP, VEC>(acc, G);
-            if constexpr (OP == OP_SOFTMAX) {
-              if (active) {
-                float ref[VEC], inv[VEC];
-                stats_of<VEC>(acc, ref, inv);
-                normalize_rows<T, VEC>(rows, out, d, col, begin, end, q, warp_step, ref, inv);
-              }
-            } else if (q == 0 && active) {
-              float y[VEC];
-              acc.result(y);
-              VecIO<T, VEC>::store(out + seg * d + col, y);
-            }
-          }
-        } else {
-          // ---- CTA class: one team
+        const int owner = span > 0 ? static_cast<int>(((begin + end - 2 * r0) * kPipeTeamWarps) / (2 * span)) : 0;
+        if ((owner < kPipeTeamWarps ? owner : kPipeTeamWarps - 1) == wit) {
           Acc<OP, VEC> acc;
           acc.init();
-          if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, team_lane, team_step);
-          team_merge<OP, VEC>(acc, part, team, wit, q, cl, G);
-          const Acc<OP, VEC> &fin = acc;
+          if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, q, warp_step);
+          warp_merge<OP, VEC>(acc, G);
           if constexpr (OP == OP_SOFTMAX) {
             if (active) {
               float ref[VEC], inv[VEC];
-              stats_of<VEC>(fin, ref, inv);
-              normalize_rows<T, VEC>(rows, out, d, col, begin, end, team_lane, team_step, ref, inv);
+              stats_of<VEC>(acc, ref, inv);
+              normalize_rows<T, VEC>(rows, out, d, col, begin, end, q, warp_step, ref, inv);
             }
-          } else if (wit == 0 && q == 0 && active) {
+          } else if (q == 0 && active) {
             float y[VEC];
-            fin.result(y);
+            acc.result(y);
             VecIO<T, VEC>::store(out + seg * d + col, y);
           }
         }
