@@ -37,6 +37,14 @@ TERMS = 6
 DEFAULTS = {"reduce": "rowbalanced", "softmax": "classified"}
 
 
+# Softmax rows narrower than this take no row-balanced schedule from the
+# cost model: with one lane per row its segment walk loads one segment end
+# per step, and runs of empty segments (1.7M of them in one B200
+# calibration case) made it 400x slower than the classified schedule, a
+# cost the linear model cannot see.  select="rowbalanced" still runs it.
+NARROW_SOFTMAX_BYTES = 64
+
+
 def family(op: str) -> str:
     return "softmax" if op == "softmax" else "reduce"
 
@@ -95,6 +103,8 @@ class CostModel:
         """The schedule to run and the predictions behind it."""
         fam = family(op)
         candidates = [s for s in (available or SCHEDULES) if s in self.coefficients[fam]]
+        if fam == "softmax" and d * element_bytes < NARROW_SOFTMAX_BYTES and len(candidates) > 1:
+            candidates = [s for s in candidates if s != "rowbalanced"] or candidates
         default = DEFAULTS[fam] if DEFAULTS[fam] in candidates else candidates[0]
         if max_len is None:
             return default, {"max_len": None, "reason": "no length statistics on the host"}
