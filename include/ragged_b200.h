@@ -206,6 +206,31 @@ int rg_run_shard(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64
 int rg_shard_combine(int op, int dtype, int64_t d, int world, int rank, const void *gathered, void *out,
                      uint32_t flags, void *stream);
 
+/* Sharded softmax (this build's multi-GPU extension; no counterpart in the
+ * reference, which runs one device): rank r normalises its own rows
+ * [row0, row1) into out (its rows only).  rg_shard_segments gives, from host
+ * offsets, the window's segments [seg0, seg1) (those whose end the window
+ * consumes, plus the one open at its end), whose statistics the rank keeps
+ * (2 D floats each) in its workspace.  rg_run_shard_softmax computes them
+ * and the edge record (reference and mass pieces of the segments cut at the
+ * window's edges, rg_shard_edge_bytes(RG_OP_SOFTMAX, d) bytes); after the
+ * all-gather, rg_shard_softmax_finish merges, in rank order, the cut
+ * segments' pieces from every rank's record and normalises the window's
+ * rows.  The workspace must persist between the two phases. */
+int rg_shard_segments(const void *offsets_host, int index_dtype, int64_t b, int world, int rank,
+                      const int64_t *splits, int64_t *seg0, int64_t *seg1);
+int rg_shard_softmax_workspace_bytes(int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world,
+                                     int rank, const int64_t *splits, int64_t seg0, int64_t seg1, uint32_t flags,
+                                     int64_t *bytes);
+int rg_run_shard_softmax(int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world, int rank,
+                         const int64_t *splits, int64_t seg0, int64_t seg1, const void *values,
+                         const void *offsets, void *edges, void *workspace, int64_t workspace_bytes,
+                         uint32_t flags, void *stream, rg_report *report);
+int rg_shard_softmax_finish(int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, int world, int rank,
+                            const int64_t *splits, int64_t seg0, int64_t seg1, const void *values,
+                            const void *offsets, const void *gathered, void *out, void *workspace,
+                            int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report);
+
 /* Row-balanced segmented sum or max that allocates nothing and takes no
  * workspace: for callers that may not allocate device memory (a host that
  * reserves all device memory for its own pool, a plugin callback that may

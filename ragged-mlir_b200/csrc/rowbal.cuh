@@ -230,6 +230,11 @@ __device__ int64_t path_search(const OffT *offsets, int64_t b, int64_t diag, int
   return lo;
 }
 
+// Whether segment `seg` has a slot in [seg0, seg1) (seg1 == 0: every one).
+__device__ __forceinline__ bool has_slot(int64_t seg, int64_t seg0, int64_t seg1) {
+  return seg1 == 0 || (seg >= seg0 && seg < seg1);
+}
+
 // Combine `count` consecutive units' pieces in row order, for one column
 // lane.  piece(k, slot) points at unit k's slot (0 = HEAD, 1 = TAIL or
 // THROUGH) for this lane, `pstride` floats between its s and c halves.  A
@@ -241,7 +246,7 @@ template <typename T, int OP, int VEC, typename PieceFn>
 __device__ __forceinline__ void combine_pieces(int count, PieceFn piece, int pstride, const int64_t *heads,
                                                const int64_t *tails, const int32_t *kinds, bool active, T *out,
                                                int64_t d, int64_t col, float *head_dst, float *tail_dst,
-                                               int64_t dstride, UnitMeta *m) {
+                                               int64_t dstride, UnitMeta *m, int64_t seg0, int64_t seg1) {
   using Acc = RowAcc<OP, VEC>;
   Acc carry;
   carry.init();
@@ -257,7 +262,7 @@ __device__ __forceinline__ void combine_pieces(int count, PieceFn piece, int pst
         here = false;
       }
       if (here) {
-        if (active) emit<T, OP, VEC>(carry, out, h, d, col);
+        if (active && has_slot(h, seg0, seg1)) emit<T, OP, VEC>(carry, out, h - seg0, d, col);
       } else {
         if (active) carry.store_piece(head_dst, dstride);
         head_seg = h;
@@ -294,7 +299,9 @@ __device__ __forceinline__ void combine_pieces(int count, PieceFn piece, int pst
 // values[0] holding row row0 (see shard.cu).
 struct RowWindow {
   int64_t row0, row1;
-  int first;  // the first window: it also consumes the segment ends at row 0
+  int first;     // the first window: it also consumes the segment ends at row 0
+  int64_t seg0;  // softmax statistics: segment seg is written at slot seg - seg0 (0: all segments)
+  int64_t seg1;  // ... for seg0 <= seg < seg1 only (0: no bound)
 };
 
 // Segment ends at or before row `row`: the first k in [0, B] with
@@ -416,8 +423,8 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
     if (first && !first_started_here) {
       acc.store_piece(my_head, VEC);
       if (gl == 0) s_head[unit_in_cta] = seg;
-    } else if (active) {
-      emit<T, OP, VEC>(acc, out, seg, d, col);
+    } else if (active && has_slot(seg, window.seg0, window.seg1)) {
+      emit<T, OP, VEC>(acc, out, seg - window.seg0, d, col);
     }
     first = false;
     acc.init();
@@ -536,7 +543,7 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
     auto piece = [&](int k, int slot) { return &s_piece[slot][((k << g_shift) + c_lane) * VEC * W]; };
     combine_pieces<T, OP, VEC>(units_per_cta, piece, VEC, s_head, s_tail, s_kind, c_cv < vec_cols, out, d, c_col,
                                cta_pieces + c_col, cta_pieces + W * d + c_col, d,
-                               tile == 0 && c_lane == 0 ? &meta[vcta] : nullptr);
+                               tile == 0 && c_lane == 0 ? &meta[vcta] : nullptr, window.seg0, window.seg1);
   }
     if (!work) break;
     __syncthreads();  // the combine is done with the shared pieces before the next virtual CTA
@@ -673,7 +680,7 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
     auto piece = [&](int k, int slot) { return &s_piece[slot][(base + k) * DS * W]; };
     UnitMeta m;
     combine_pieces<T, OP, DS>(32, piece, DS, s_head + base, s_tail + base, s_kind + base, true, out, DS, 0,
-                              &w_piece[0][warp * DS * W], &w_piece[1][warp * DS * W], DS, &m);
+                              &w_piece[0][warp * DS * W], &w_piece[1][warp * DS * W], DS, &m, 0, 0);
     w_head[warp] = m.head_seg;
     w_tail[warp] = m.tail_seg;
     w_kind[warp] = m.tail_kind;
@@ -684,7 +691,7 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
     auto piece = [&](int k, int slot) { return &w_piece[slot][k * DS * W]; };
     float *const cta_pieces = pieces + static_cast<int64_t>(blockIdx.x) * 2 * W * DS;
     combine_pieces<T, OP, DS>(NW, piece, DS, w_head, w_tail, w_kind, true, out, DS, 0, cta_pieces,
-                              cta_pieces + W * DS, DS, &meta[blockIdx.x]);
+                              cta_pieces + W * DS, DS, &meta[blockIdx.x], 0, 0);
   }
 }
 
@@ -781,7 +788,8 @@ __device__ __forceinline__ int64_t find_head(const UnitMeta *__restrict__ meta, 
 template <typename T, int OP, int VEC>
 __global__ void __launch_bounds__(kFixupThreads)
 rowbal_fixup_kernel(T *__restrict__ out, int64_t d, int vec_cols, int64_t units,
-                    const float *__restrict__ pieces, const UnitMeta *__restrict__ meta, float *__restrict__ edges) {
+                    const float *__restrict__ pieces, const UnitMeta *__restrict__ meta, float *__restrict__ edges,
+                    int64_t seg0 = 0, int64_t seg1 = 0) {
   using Acc = RowAcc<OP, VEC>;
   constexpr int NW = kFixupThreads / 32;
   __shared__ int64_t s_end;
@@ -826,7 +834,38 @@ rowbal_fixup_kernel(T *__restrict__ out, int64_t d, int vec_cols, int64_t units,
     return;
   }
   chain_merge<OP, VEC>(total, pieces, meta, d, col, active, u, end, true, s_part);
-  if (warp == 0 && active) emit<T, OP, VEC>(total, out, seg, d, col);
+  if (warp == 0 && active && has_slot(seg, seg0, seg1)) emit<T, OP, VEC>(total, out, seg - seg0, d, col);
+}
+
+// Softmax of a sharded call: the final statistics of the segments cut at
+// this rank's edges (the one open at its first row, the one open at its
+// last), merged in rank order from every rank's edge record -- a starting
+// rank's TAIL piece, then HEAD pieces of the ranks the segment passes
+// through or ends in -- into this rank's slots (segment s at s - seg0).
+// Every rank holding rows of a cut segment computes the same statistics.
+template <int VEC>
+__global__ void __launch_bounds__(32)
+shard_softmax_combine_kernel(float *__restrict__ stats, int64_t d, int vec_cols, int world, int rank,
+                             const float *__restrict__ gathered, int64_t seg0, int64_t seg1) {
+  using Acc = RowAcc<OP_SOFTMAX, VEC>;
+  const int64_t wd = Acc::kWidth * d;
+  const int64_t rec = edge_record_floats(wd);
+  const int cv = blockIdx.y * 32 + threadIdx.x;
+  if (cv >= vec_cols) return;
+  const int64_t col = static_cast<int64_t>(cv) * VEC;
+  const int64_t *mine = reinterpret_cast<const int64_t *>(gathered + rank * rec);
+  for (int which = 0; which < 2; ++which) {
+    const int64_t s = mine[which == 0 ? 0 : 2];
+    if (s < 0 || !has_slot(s, seg0, seg1)) continue;
+    Acc total;
+    total.init();
+    for (int k = 0; k < world; ++k) {
+      const int64_t *h = reinterpret_cast<const int64_t *>(gathered + k * rec);
+      if (h[2] == s) total.merge_piece(gathered + k * rec + kEdgeHeader + wd + col, d);  // started in rank k
+      else if (h[0] == s) total.merge_piece(gathered + k * rec + kEdgeHeader + col, d);   // open at k's start
+    }
+    total.store_piece(stats + (s - seg0) * 2 * d + col, d);
+  }
 }
 
 // Finish the segments cut by shard boundaries on the rank that consumed
@@ -877,7 +916,10 @@ template <typename T, typename OffT, int VEC, int U = 8>
 __global__ void __launch_bounds__(kRowbalThreads, 3)
 rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
                         const float *__restrict__ stats, int64_t n, int64_t b, int64_t d, int g_shift, int vec_cols,
-                        int64_t units) {
+                        int64_t units, int64_t row_base = 0, int64_t seg0 = 0, int64_t seg1 = 0) {
+  // values[i] and out[i] hold row row_base + i of the whole array (a rank's
+  // window of a sharded call; 0 otherwise); the statistics of segment s sit
+  // at slot s - seg0 (seg1: end of the slots, 0 = unbounded).
   const int lane = threadIdx.x & 31;
   const int G = 1 << g_shift;
   const int q = lane >> g_shift, gl = lane & (G - 1);
@@ -888,7 +930,7 @@ rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ o
   const int cv = blockIdx.y * 32 + gl;
   const bool active = cv < vec_cols;
   const int64_t col = static_cast<int64_t>(cv) * VEC;
-  const int64_t r0 = n / units * unit + min(unit, n % units);
+  const int64_t r0 = row_base + n / units * unit + min(unit, n % units);  // whole-array rows
   const int64_t r1 = r0 + n / units + (unit < n % units ? 1 : 0);
   if (r1 <= r0) return;  // uniform per unit; no barriers below
   // Segment of the last row: the first k with offsets[k + 1] > r1 - 1.
@@ -896,30 +938,31 @@ rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ o
   int64_t start = load_offset(offsets, seg);
   float ref[VEC], inv[VEC];
   auto load_stats = [&]() {
-    const float *st = stats + seg * 2 * d + col;
+    const bool slot = seg1 == 0 || (seg >= seg0 && seg < seg1);  // a wrong caller range: NaN, never out of bounds
+    const float *st = stats + (slot ? seg - seg0 : 0) * 2 * d + col;
 #pragma unroll
     for (int v = 0; v < VEC; ++v) {
-      ref[v] = __ldcg(st + v);
-      inv[v] = stats_inverse(__ldcg(st + d + v));
+      ref[v] = slot ? __ldcg(st + v) : __int_as_float(0x7fffffff);
+      inv[v] = slot ? stats_inverse(__ldcg(st + d + v)) : __int_as_float(0x7fffffff);
     }
   };
   if (active) load_stats();
   using Raw = typename VecIO<T, VEC>::Raw;
-  const T *const src = values + col;
+  const T *const src = values + col;  // row r sits at (r - row_base) * d
   T *const dst = out + col;
   auto normalize_row = [&](const Raw &raw, int64_t r) {
     float x[VEC], y[VEC];
     VecIO<T, VEC>::unpack(raw, x);
 #pragma unroll
     for (int v = 0; v < VEC; ++v) y[v] = stats_normalize(x[v], ref[v], inv[v]);
-    VecIO<T, VEC>::store(dst + r * d, y);
+    VecIO<T, VEC>::store(dst + (r - row_base) * d, y);
   };
   int64_t r = r1 - 1;
   for (; r - (U - 1) >= r0; r -= U) {
     Raw raw[U];
 #pragma unroll
     for (int t = 0; t < U; ++t)
-      if (active) raw[t] = VecIO<T, VEC>::load_raw(src + (r - t) * d);
+      if (active) raw[t] = VecIO<T, VEC>::load_raw(src + (r - t - row_base) * d);
 #pragma unroll
     for (int t = 0; t < U; ++t) {
       while (r - t < start) {  // the previous segment (skipping empty ones)
@@ -936,7 +979,7 @@ rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ o
       start = load_offset(offsets, seg);
       if (r >= start && active) load_stats();
     }
-    if (active) normalize_row(VecIO<T, VEC>::load_raw(src + r * d), r);
+    if (active) normalize_row(VecIO<T, VEC>::load_raw(src + (r - row_base) * d), r);
   }
 }
 

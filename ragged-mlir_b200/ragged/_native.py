@@ -30,7 +30,7 @@ MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.
 EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
-            "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_pointwise_workspace_bytes", "rg_run_pointwise", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
+            "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_pointwise_workspace_bytes", "rg_run_pointwise", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes", "rg_shard_segments", "rg_shard_softmax_workspace_bytes", "rg_run_shard_softmax", "rg_shard_softmax_finish",
             "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
 
 
@@ -105,6 +105,16 @@ def library(path: Path | None = None):
         lib.rg_run_shard.restype = i32
         lib.rg_shard_combine.argtypes = [i32, i32, i64, i32, i32, p, p, u32, p]
         lib.rg_shard_combine.restype = i32
+        lib.rg_shard_segments.argtypes = [p, i32, i64, i32, i32, pi64, pi64, pi64]
+        lib.rg_shard_segments.restype = i32
+        lib.rg_shard_softmax_workspace_bytes.argtypes = [i32, i32, i64, i64, i64, i32, i32, pi64, i64, i64, u32, pi64]
+        lib.rg_shard_softmax_workspace_bytes.restype = i32
+        lib.rg_run_shard_softmax.argtypes = [i32, i32, i64, i64, i64, i32, i32, pi64, i64, i64, p, p, p, p, i64, u32,
+                                             p, ctypes.POINTER(Report)]
+        lib.rg_run_shard_softmax.restype = i32
+        lib.rg_shard_softmax_finish.argtypes = [i32, i32, i64, i64, i64, i32, i32, pi64, i64, i64, p, p, p, p, p, i64,
+                                                u32, p, ctypes.POINTER(Report)]
+        lib.rg_shard_softmax_finish.restype = i32
         _lib = lib
         return lib
 
@@ -243,6 +253,53 @@ def shard_combine(op: str, dtype: str, d: int, world: int, rank: int, gathered_p
                   stream: int) -> None:
     raise_for(library().rg_shard_combine(OPS[op], DTYPES[dtype], d, world, rank, gathered_ptr, out_ptr, flags,
                                          stream or None), "rg_shard_combine")
+
+
+def shard_segments(offsets_host, index: str, world: int, rank: int, splits=None) -> tuple[int, int]:
+    """Segments [seg0, seg1) whose softmax statistics rank `rank` keeps."""
+    import numpy as np
+    offs = np.ascontiguousarray(offsets_host, dtype=np.int32 if index == "i32" else np.int64)
+    seg0, seg1 = ctypes.c_int64(0), ctypes.c_int64(0)
+    arg = _splits_arg(splits)
+    raise_for(library().rg_shard_segments(offs.ctypes.data, INDEX[index], offs.size - 1, world, rank,
+                                          arg[0] if arg else None, ctypes.byref(seg0), ctypes.byref(seg1)),
+              "rg_shard_segments")
+    return int(seg0.value), int(seg1.value)
+
+
+def shard_softmax_workspace_bytes(dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int,
+                                  segments: tuple[int, int], flags: int = 0, splits=None) -> int:
+    out = ctypes.c_int64(0)
+    arg = _splits_arg(splits)
+    raise_for(library().rg_shard_softmax_workspace_bytes(DTYPES[dtype], INDEX[index], d, n, b, world, rank,
+                                                         arg[0] if arg else None, segments[0], segments[1], flags,
+                                                         ctypes.byref(out)), "rg_shard_softmax_workspace_bytes")
+    return int(out.value)
+
+
+def run_shard_softmax(dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int,
+                      segments: tuple[int, int], values_ptr: int, offsets_ptr: int, edges_ptr: int, workspace_ptr: int,
+                      workspace_bytes: int, flags: int, stream: int, splits=None) -> Report:
+    report = Report()
+    arg = _splits_arg(splits)
+    raise_for(library().rg_run_shard_softmax(DTYPES[dtype], INDEX[index], d, n, b, world, rank,
+                                             arg[0] if arg else None, segments[0], segments[1], values_ptr or None,
+                                             offsets_ptr, edges_ptr, workspace_ptr or None, workspace_bytes, flags,
+                                             stream or None, ctypes.byref(report)), "rg_run_shard_softmax")
+    return report
+
+
+def shard_softmax_finish(dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int,
+                         segments: tuple[int, int], values_ptr: int, offsets_ptr: int, gathered_ptr: int, out_ptr: int,
+                         workspace_ptr: int, workspace_bytes: int, flags: int, stream: int, splits=None) -> Report:
+    report = Report()
+    arg = _splits_arg(splits)
+    raise_for(library().rg_shard_softmax_finish(DTYPES[dtype], INDEX[index], d, n, b, world, rank,
+                                                arg[0] if arg else None, segments[0], segments[1],
+                                                values_ptr or None, offsets_ptr, gathered_ptr, out_ptr or None,
+                                                workspace_ptr or None, workspace_bytes, flags, stream or None,
+                                                ctypes.byref(report)), "rg_shard_softmax_finish")
+    return report
 
 
 def check_offsets(index: str, n: int, b: int, offsets_ptr: int, min_len: int | None, max_len: int | None,

@@ -277,20 +277,23 @@ class CompiledProgram:
         return report, (time.perf_counter() - started) * 1000
 
     def run_sharded(self, values, offsets, out, *, total_rows: int, world: int, rank: int, exchange,
-                    stream=None, splits=None) -> ExecutionReport:
-        """One rank's part of a row-sharded sum or max (``ragged.sharding``).
+                    stream=None, splits=None, offsets_host=None) -> ExecutionReport:
+        """One rank's part of a row-sharded call (``ragged.sharding``).
 
         ``values`` holds this rank's rows ``sharding.shard_rows(total_rows,
         world, rank, splits)`` of a call over ``total_rows`` rows (``splits``:
         world + 1 row boundaries, e.g. ``sharding.balanced_split``; None: the
-        even row split), ``offsets`` all B+1 entries, ``out`` all B
-        output rows (only the rows this rank finishes are written:
-        ``sharding.segment_owners``).  ``exchange(edges)`` must return the
-        edge records of ranks 0..world-1 concatenated (an all-gather); it is
-        the only communication.  Launches on ``stream`` (default: current),
-        no host synchronisation of its own."""
-        if self.spec.op not in ("sum", "max"):
-            raise RuntimeUnavailable("sharded calls compute sum and max in this build")
+        even row split), ``offsets`` all B+1 entries.  Sum and max: ``out``
+        holds all B output rows (only the rows this rank finishes are
+        written: ``sharding.segment_owners``).  Softmax: ``out`` holds this
+        rank's rows, and ``offsets_host`` (the offsets in host memory) gives
+        the segments whose statistics the rank keeps.  ``exchange(edges)``
+        must return the edge records of ranks 0..world-1 concatenated (an
+        all-gather); it is the only communication.  Launches on ``stream``
+        (default: current), no host synchronisation of its own."""
+        if self.spec.op == "softmax":
+            return self._run_sharded_softmax(values, offsets, out, total_rows, world, rank, exchange, stream, splits,
+                                             offsets_host)
         if self._pointwise:
             raise RuntimeUnavailable("sharded calls take no scale (the input transform is single-GPU only)")
         torch = _torch()
@@ -335,6 +338,63 @@ class CompiledProgram:
         result = self._report("rowbalanced", {"sharded": {"world": world, "rank": rank, "rows": [row0, row1]}},
                               started, report, nbytes)
         return result
+
+    def _run_sharded_softmax(self, values, offsets, out, total_rows, world, rank, exchange, stream, splits,
+                             offsets_host):
+        """Softmax of a row-sharded call: statistics of the rank's window and
+        its edge record, the all-gather, then the merged statistics of the
+        cut segments and the window's rows normalised into ``out``."""
+        if self._pointwise:
+            raise RuntimeUnavailable("sharded calls take no scale or mask (the input transform is single-GPU only)")
+        if offsets_host is None:
+            raise ValidationError("sharded softmax needs offsets_host (the offsets in host memory)")
+        torch = _torch()
+        if not 0 <= rank < world:
+            raise ValidationError("need 0 <= rank < world")
+        from .sharding import shard_rows
+        row0, row1 = shard_rows(total_rows, world, rank, splits)
+        for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
+            if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
+                raise RuntimeUnavailable(f"{name} must be a CUDA tensor; no CPU execution fallback exists")
+            if not tensor.is_contiguous():
+                raise ValidationError(f"{name} must be row-major contiguous")
+        d = self.spec.feature_dim
+        b = offsets.numel() - 1
+        rows = (row1 - row0, d)
+        if tuple(values.shape) != rows or tuple(out.shape) != rows:
+            raise ValidationError(f"values and out must hold this rank's {row1 - row0} rows: shape {rows}")
+        dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype]
+        offset_dtype = {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype]
+        if values.dtype != dtype or out.dtype != dtype or offsets.dtype != offset_dtype:
+            raise ValidationError("tensor dtype differs from compiled dtype/offsets specialization")
+        if len(offsets_host) != b + 1:
+            raise ValidationError("offsets_host must hold the same B+1 offsets")
+        spec = self.spec
+        segments = _native.shard_segments(offsets_host, spec.offsets_dtype, world, rank, splits)
+        started = time.perf_counter()
+        with torch.cuda.device(values.device):
+            active = stream if stream is not None else torch.cuda.current_stream(values.device)
+            nbytes = _native.shard_softmax_workspace_bytes(spec.dtype, spec.offsets_dtype, d, total_rows, b, world,
+                                                           rank, segments, self._flags, splits)
+            with torch.cuda.stream(active):
+                scratch = torch.empty((max(nbytes, 1),), dtype=torch.uint8, device=values.device)
+                edges = torch.empty((_native.shard_edge_bytes("softmax", d) // 4,), dtype=torch.float32,
+                                    device=values.device)
+                ptr = values.data_ptr() if values.numel() else 0
+                first = _native.run_shard_softmax(spec.dtype, spec.offsets_dtype, d, total_rows, b, world, rank,
+                                                  segments, ptr, offsets.data_ptr(), edges.data_ptr(),
+                                                  scratch.data_ptr(), nbytes, self._flags, active.cuda_stream, splits)
+                gathered = exchange(edges)
+                if gathered.numel() != world * edges.numel() or gathered.device != values.device:
+                    raise ValidationError("exchange must return every rank's edge record on this device")
+                report = _native.shard_softmax_finish(spec.dtype, spec.offsets_dtype, d, total_rows, b, world, rank,
+                                                      segments, ptr, offsets.data_ptr(), gathered.data_ptr(),
+                                                      out.data_ptr() if out.numel() else 0, scratch.data_ptr(),
+                                                      nbytes, self._flags, active.cuda_stream, splits)
+        names = tuple(_native.kernel_name(first.kernel_ids[i]) for i in range(first.num_launches))
+        result = self._report("rowbalanced", {"sharded": {"world": world, "rank": rank, "rows": [row0, row1],
+                                                          "segments": list(segments)}}, started, report, nbytes)
+        return replace(result, kernel_names=names + result.kernel_names)
 
     def _report(self, schedule, selection, started, report, nbytes, validation=None) -> ExecutionReport:
         validation, validation_ms = validation if validation is not None else (None, None)

@@ -1,15 +1,18 @@
 """Row-sharded calls across the GPUs of one node (one process per GPU).
 
 The reference runs one program on one device (README.md:457-461); this
-build adds a sharded form of the row-balanced sum and max for inputs that
-are spread over several GPUs.  Rank r of ``world`` holds rows
+build adds a sharded form of the row-balanced sum, max and softmax for
+inputs that are spread over several GPUs.  Rank r of ``world`` holds rows
 ``shard_rows(N, world, r)`` of the packed values and the whole offsets
 array.  Every rank reduces its rows; a segment cut by a shard boundary
 leaves f32 pieces in the rank's edge record; the ranks all-gather the
 records (NCCL over NVLink through ``torch.distributed``: a few KB per rank,
 the only collective of the path); and the rank that holds a cut segment's
 end merges its pieces in rank order.  Each output row is written by exactly
-one rank: ``segment_owners`` says which.
+one rank: ``segment_owners`` says which.  Softmax: every rank normalises
+its own rows; the (reference, mass) pieces of the segments cut at its edges
+are merged from all ranks' records in rank order on every rank that holds
+rows of them.
 
 ``ShardedProgram`` wraps a compiled sum or max program for one rank;
 ``CompiledProgram.run_sharded`` is the call it makes.
@@ -107,6 +110,7 @@ class ShardedProgram:
     def rows(self, n: int) -> tuple[int, int]:
         return shard_rows(n, self.world, self.rank, self.splits)
 
-    def run(self, values, offsets, out, *, total_rows: int, stream=None):
+    def run(self, values, offsets, out, *, total_rows: int, stream=None, offsets_host=None):
         return self.program.run_sharded(values, offsets, out, total_rows=total_rows, world=self.world, rank=self.rank,
-                                        exchange=torch_exchange(self.group), stream=stream, splits=self.splits)
+                                        exchange=torch_exchange(self.group), stream=stream, splits=self.splits,
+                                        offsets_host=offsets_host)

@@ -136,3 +136,95 @@ def test_sharded_balanced_split(cuda, op, world):
     values = prepared(np.random.default_rng(world).normal(size=(int(offsets[-1]), 64)), "bf16")
     actual = run_world(cuda, op, "bf16", values, offsets, world, splits)
     check(actual, values, offsets, op, "bf16")
+
+
+# ---------------------------------------------------------------- softmax
+
+def run_world_softmax(torch, dtype, values, offsets, world, splits=None):
+    """Every rank's statistics phase, the gathered edge records, then every
+    rank's finishing phase; the ranks' rows concatenated."""
+    from ragged import _native
+    from ragged.sharding import shard_rows
+    d = values.shape[1]
+    n, b = int(offsets[-1]), offsets.size - 1
+    index = "i32" if offsets.dtype == np.int32 else "i64"
+    tdtype = torch.float32 if dtype == "f32" else torch.bfloat16
+    stream = torch.cuda.current_stream().cuda_stream
+    dev_values = torch.from_numpy(np.ascontiguousarray(values, dtype=np.float32)).to("cuda").to(tdtype)
+    dev_offsets = torch.from_numpy(offsets).to("cuda")
+    edges = torch.empty((world, _native.shard_edge_bytes("softmax", d) // 4), dtype=torch.float32, device="cuda")
+    ranks = []
+    covered = np.zeros(b, dtype=bool)
+    for rank in range(world):
+        row0, row1 = shard_rows(n, world, rank, splits)
+        seg0, seg1 = _native.shard_segments(offsets, index, world, rank, splits)
+        # every segment with rows in the window has a statistics slot
+        for s in range(b):
+            if offsets[s] < row1 and offsets[s + 1] > row0 and offsets[s + 1] > offsets[s]:
+                assert seg0 <= s < seg1, (rank, s, seg0, seg1)
+                covered[s] = True
+        local = dev_values[row0:row1].contiguous()
+        ws = _native.shard_softmax_workspace_bytes(dtype, index, d, n, b, world, rank, (seg0, seg1), 0, splits)
+        scratch = torch.empty((max(ws, 1),), dtype=torch.uint8, device="cuda")
+        _native.run_shard_softmax(dtype, index, d, n, b, world, rank, (seg0, seg1),
+                                  local.data_ptr() if local.numel() else 0, dev_offsets.data_ptr(),
+                                  edges[rank].data_ptr(), scratch.data_ptr(), ws, 0, stream, splits)
+        ranks.append((row0, row1, (seg0, seg1), local, ws, scratch))
+    gathered = edges.reshape(-1).contiguous()
+    guard = torch.full((n + 2, d), SENTINEL, dtype=tdtype, device="cuda")
+    for rank, (row0, row1, segments, local, ws, scratch) in enumerate(ranks):
+        out = guard[1 + row0:1 + row1]
+        _native.shard_softmax_finish(dtype, index, d, n, b, world, rank, segments,
+                                     local.data_ptr() if local.numel() else 0, dev_offsets.data_ptr(),
+                                     gathered.data_ptr(), out.data_ptr() if out.numel() else 0, scratch.data_ptr(),
+                                     ws, 0, stream, splits)
+    torch.cuda.synchronize()
+    host = guard.float().cpu().numpy().astype(np.float64)
+    assert np.all(host[0] == SENTINEL) and np.all(host[-1] == SENTINEL), "write outside the rows"
+    return host[1:-1]
+
+
+@pytest.mark.parametrize("dtype,d", [("f32", 128), ("bf16", 256), ("f32", 3), ("bf16", 64)])
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("balanced", [False, True])
+def test_sharded_softmax_matches_oracle(cuda, dtype, d, world, balanced):
+    from ragged.sharding import balanced_split
+    rng = np.random.default_rng(2000 + world + d)
+    lengths = make_lengths("long_tail", 400, 60_000 if d <= 128 else 20_000, seed=world + 7)
+    lengths[5] = 0
+    lengths[-1] = 0
+    offsets = offsets_of(lengths)
+    values = prepared(rng.normal(scale=2.0, size=(int(offsets[-1]), d)), dtype)
+    values[rng.random(values.shape) < 1e-4] = np.nan
+    splits = balanced_split(offsets, world) if balanced else None
+    actual = run_world_softmax(cuda, dtype, values, offsets, world, splits)
+    check(actual, values, offsets, "softmax", dtype)
+
+
+def test_sharded_softmax_segment_through_whole_shards(cuda):
+    """One segment covers several whole shards (through windows); a late
+    maximum on a middle rank rescales every other rank's piece."""
+    lengths = np.array([3, 50_000, 0, 7, 1], dtype=np.int64)
+    offsets = offsets_of(lengths, "i32")
+    values = prepared(np.random.default_rng(91).normal(size=(int(offsets[-1]), 64)), "bf16")
+    values[30_000, 7] = 25.0
+    actual = run_world_softmax(cuda, "bf16", values, offsets, 8)
+    check(actual, values, offsets, "softmax", "bf16")
+
+
+def test_sharded_softmax_through_the_runtime(cuda):
+    """CompiledProgram.run_sharded on one rank of a world of one (the
+    exchange is the identity)."""
+    torch = cuda
+    from helpers import program
+    lengths = make_lengths("bimodal", 300, 40_000, seed=92)
+    offsets = offsets_of(lengths)
+    values = np.random.default_rng(93).normal(size=(int(offsets[-1]), 32)).astype(np.float32)
+    dv = torch.from_numpy(values).cuda()
+    out = torch.empty_like(dv)
+    report = program("softmax", "f32", 32, "i64").run_sharded(
+        dv, torch.from_numpy(offsets).cuda(), out, total_rows=int(offsets[-1]), world=1, rank=0,
+        exchange=lambda edges: edges, offsets_host=offsets)
+    torch.cuda.synchronize()
+    assert "rowbalanced_normalize" in report.kernel_names
+    check(out.cpu().numpy().astype(np.float64), values, offsets, "softmax", "f32")

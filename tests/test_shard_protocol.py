@@ -171,3 +171,159 @@ def test_shard_rows_matches_native_library():
             for rank in range(world):
                 assert shard_rows(n, world, rank) == _native.shard_rows(n, world, rank)
     assert _native.shard_edge_bytes("sum", 256) % 16 == 0 and _native.shard_edge_bytes("max", 3) % 16 == 0
+
+
+# ---------------------------------------------------------------- softmax
+#
+# Each rank keeps (reference m, mass s) statistics, s relative to m, for the
+# segments finished in its rows; the segment open at its first row (HEAD, or
+# THROUGH when it covers every row) and the one that starts in its rows and is
+# open at its last (TAIL) go to its edge record.  After the all-gather every
+# rank merges, in rank order, the pieces of ITS cut segments from all ranks'
+# records (a starting rank's TAIL piece, then the pieces of the ranks the
+# segment covers) and normalises its own rows.
+
+def _stats(rows):
+    d = rows.shape[1]
+    if rows.shape[0] == 0:
+        return np.full(d, -np.inf), np.zeros(d)
+    with np.errstate(all="ignore"):
+        m = rows.max(axis=0)
+        m[np.isnan(rows).any(axis=0)] = np.nan
+        base = np.where(m == -np.inf, 0.0, m)
+        s = np.exp(rows - base).sum(axis=0)
+    return m, s
+
+
+def _smerge(a, b):
+    (ma, sa), (mb, sb) = a, b
+    with np.errstate(all="ignore"):
+        m = np.fmax(ma, mb)
+        m[np.isnan(ma) | np.isnan(mb)] = np.nan
+        ta = np.where(ma == -np.inf, 0.0, sa * np.exp(ma - m))
+        tb = np.where(mb == -np.inf, 0.0, sb * np.exp(mb - m))
+    return m, ta + tb
+
+
+def rank_part_softmax(values_local, offsets, row0, row1, rank):
+    """(statistics of segments finished here, edge record) of one window."""
+    b = offsets.size - 1
+    d = values_local.shape[1]
+    ends = offsets[1:]
+    lo = 0 if rank == 0 else int(np.searchsorted(ends, row0, side="right"))
+    hi = int(np.searchsorted(ends, row1, side="right"))
+    stats, head_seg, head_ends, head = {}, -1, 0, None
+    for s in range(lo, hi):
+        start, end = int(offsets[s]), int(offsets[s + 1])
+        piece = _stats(values_local[max(start, row0) - row0:end - row0])
+        if start >= row0:
+            stats[s] = piece
+        else:
+            head_seg, head_ends, head = s, 1, piece
+    tail_seg, tail = -1, None
+    if hi < b and row1 > row0 and int(offsets[hi]) < row1:
+        s, start = hi, int(offsets[hi])
+        piece = _stats(values_local[max(start, row0) - row0:row1 - row0])
+        if start >= row0:
+            tail_seg, tail = s, piece
+        elif head_seg < 0:
+            head_seg, head_ends, head = s, 0, piece
+    ident = (np.full(d, -np.inf), np.zeros(d))
+    head, tail = head or ident, tail or ident
+    return stats, np.concatenate([[head_seg, head_ends, tail_seg], head[0], head[1], tail[0], tail[1]])
+
+
+def finish_softmax(values_local, offsets, row0, row1, rank, stats, records):
+    d = values_local.shape[1]
+    own = records[rank]
+    for s in (int(own[0]), int(own[2])):
+        if s < 0:
+            continue
+        total = (np.full(d, -np.inf), np.zeros(d))
+        for rec in records:
+            if int(rec[2]) == s:
+                total = _smerge(total, (rec[3 + 2 * d:3 + 3 * d], rec[3 + 3 * d:3 + 4 * d]))
+            elif int(rec[0]) == s:
+                total = _smerge(total, (rec[3:3 + d], rec[3 + d:3 + 2 * d]))
+        stats[s] = total
+    out = np.empty_like(values_local)
+    for s in range(offsets.size - 1):
+        start, end = max(int(offsets[s]), row0), min(int(offsets[s + 1]), row1)
+        if start >= end:
+            continue
+        m, t = stats[s]
+        with np.errstate(all="ignore"):
+            base = np.where(m == -np.inf, 0.0, m)
+            out[start - row0:end - row0] = np.exp(values_local[start - row0:end - row0] - base) / t
+    return out
+
+
+def _softmax_worker(rank, world, port, cases, results):
+    import torch
+    import torch.distributed as dist
+    from ragged.sharding import balanced_split, shard_rows
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        out = []
+        for values, offsets, balanced in cases:
+            n = int(offsets[-1])
+            splits = balanced_split(offsets, world) if balanced else None
+            row0, row1 = shard_rows(n, world, rank, splits)
+            local = values[row0:row1]
+            stats, record = rank_part_softmax(local, offsets, row0, row1, rank)
+            mine = torch.from_numpy(record)
+            gathered = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(gathered, mine)
+            out.append((row0, finish_softmax(local, offsets, row0, row1, rank, stats, [g.numpy() for g in gathered])))
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_softmax_protocol_over_gloo(world):
+    import torch.multiprocessing as mp
+    from oracle import reference_port as rp
+    rng = np.random.default_rng(8)
+    cases = []
+    lengths = make_lengths("long_tail", 60, 5000, seed=4)
+    offsets = offsets_of(lengths)
+    cases.append((rng.normal(scale=3.0, size=(int(offsets[-1]), 4)), offsets))
+    lengths = np.array([0, 3, 997, 0, 0, 1500, 498, 2, 0], dtype=np.int64)
+    offsets = offsets_of(lengths)
+    values = rng.normal(size=(int(offsets[-1]), 3))
+    values[10, 1] = np.nan
+    values[1200:1300, 2] = -np.inf
+    cases.append((values, offsets))
+    cases = [(v, o, balanced) for v, o in cases for balanced in (False, True)]
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_softmax_worker, args=(world, _free_port(), cases, results), nprocs=world, start_method="spawn")
+    for i, (values, offsets, _) in enumerate(cases):
+        parts = sorted(results[rank][i] for rank in range(world))
+        actual = np.concatenate([p[1] for p in parts], axis=0)
+        with np.errstate(all="ignore"):
+            expected = rp.segment_softmax(values, offsets)
+        np.testing.assert_allclose(actual, expected, rtol=1e-12, atol=1e-15, equal_nan=True)
+
+
+def test_shard_segments_cover_every_window_row():
+    """rg_shard_segments (host code, no GPU): the statistics slots of a rank
+    cover every segment with rows in its window, for even and balanced
+    splits, with empty segments at the boundaries."""
+    from ragged import _native
+    from ragged.sharding import balanced_split, shard_rows
+    lengths = np.array([0, 0, 5, 0, 100, 1, 0, 0, 37, 400, 0, 2, 0], dtype=np.int64)
+    offsets = offsets_of(lengths)
+    n, b = int(offsets[-1]), offsets.size - 1
+    for world in (1, 2, 3, 5, 8):
+        for splits in (None, balanced_split(offsets, world)):
+            for rank in range(world):
+                row0, row1 = shard_rows(n, world, rank, splits)
+                seg0, seg1 = _native.shard_segments(offsets, "i64", world, rank, splits)
+                assert 0 <= seg0 <= seg1 <= b
+                for s in range(b):
+                    if offsets[s] < row1 and offsets[s + 1] > row0:
+                        assert seg0 <= s < seg1, (world, rank, s, seg0, seg1)
