@@ -12,9 +12,9 @@
 // consecutive stages for one team.  So every row is read from HBM once by the worker; for softmax the
 // statistics and the normalisation both read shared memory.
 //
-// Each stage belongs to one team of 4 consumer warps (the producer rotates
-// the teams), so three stages are reduced at once and a team's barriers
-// never wait on another team.  Every segment of a run goes to ONE warp of
+// Each stage belongs to one team of 2 consumer warps (the producer rotates
+// the four teams over the four stages), so four stages are reduced at once
+// and a team's barriers never wait on another team.  Every segment of a run goes to ONE warp of
 // the team (shuffles only, no barrier): the warps take contiguous groups of
 // the run's segments with about equal rows.  (The reference splits its
 // non-split segments at 32 rows between warp and CTA workers, lib/
@@ -36,8 +36,27 @@
 
 namespace rgb {
 
-constexpr int kPipeConsumerWarps = 12;
-constexpr int kPipeTeamWarps = 4;
+// One producer warp, 8 consumer warps in 4 teams of 2, 4 stages of 56 KB:
+// on B200 the c3 softmax call (bf16, D = 128) took 205 us with this shape,
+// against 235 us for 12 consumer warps in 3 teams of 4 over 3 stages of
+// 63 KB; 5 or 6 stages, 6 teams, or 4-warp teams over 4 stages measured
+// 210-255 us (smaller stages put more segments in the split class).
+#ifndef RG_PIPE_TEAM_WARPS
+#define RG_PIPE_TEAM_WARPS 2
+#endif
+#ifndef RG_PIPE_STAGES
+#define RG_PIPE_STAGES 4
+#endif
+#ifndef RG_PIPE_CONSUMER_WARPS
+#define RG_PIPE_CONSUMER_WARPS 8
+#endif
+
+constexpr int kPipeConsumerWarps = RG_PIPE_CONSUMER_WARPS;
+constexpr int kPipeTeamWarps = RG_PIPE_TEAM_WARPS;
+static_assert(kPipeConsumerWarps % kPipeTeamWarps == 0, "teams must split the consumer warps evenly");
+// A team's row step (kPipeTeamWarps << (5 - g_shift)) must be a power of
+// two: lane_rows counts a thread's rows with a shift.
+static_assert((kPipeTeamWarps & (kPipeTeamWarps - 1)) == 0, "warps per team must be a power of two");
 constexpr int kPipeTeams = kPipeConsumerWarps / kPipeTeamWarps;
 constexpr int kPipeThreads = 32 * (kPipeConsumerWarps + 1);
 constexpr int kPipeProducer = kPipeConsumerWarps;  // warp index of the producer
@@ -45,11 +64,10 @@ constexpr int kPipeClaim = 32;                     // segments claimed per atomi
 constexpr int kSmemBudget = 227 * 1024;
 constexpr uint32_t kPieceBytes = 4096;  // bytes per bulk-copy request (a multiple of 16)
 
-// Three stages for every op: softmax measured 3% faster on B200 with three
-// stages of 63 KB (more rows fit one stage) than with four of 47 KB.
+// The same stage count for every op.
 template <int OP>
 struct PipeStages {
-  static constexpr int value = 3;
+  static constexpr int value = RG_PIPE_STAGES;
 };
 
 enum : int32_t { STAGE_RUN = 0, STAGE_SPLIT = 1, STAGE_DONE = 2 };
@@ -70,12 +88,12 @@ struct StageRecord {
 template <int OP, int VEC>
 struct PipeLayout {
   static constexpr int kStages = PipeStages<OP>::value;
-  static constexpr int kPartBytes = kPipeConsumerWarps * 32 * static_cast<int>(sizeof(Acc<OP, VEC>));
   static constexpr int kRecordBytes = kStages * static_cast<int>(sizeof(StageRecord));
   static constexpr int kBarrierBytes = 2 * kStages * 8 + 64;
-  static constexpr int kStageBytes =
-      ((kSmemBudget - kPartBytes - kRecordBytes - kBarrierBytes - 256) / kStages) / 1024 * 1024;
-  static constexpr int kTotalBytes = kStages * kStageBytes + kPartBytes + kRecordBytes + kBarrierBytes + 128;
+  static constexpr int kStageBytes = ((kSmemBudget - kRecordBytes - kBarrierBytes - 256) / kStages) / 1024 * 1024;
+  static constexpr int kTotalBytes = kStages * kStageBytes + kRecordBytes + kBarrierBytes + 128;
+  // A team merges its warps' partials in the stage it holds (team_merge).
+  static_assert(kStageBytes >= kPipeTeamWarps * 32 * static_cast<int>(sizeof(Acc<OP, VEC>)), "stage too small");
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -86,22 +104,25 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
 }
 
-// Merge the row groups of a team (kPipeTeamWarps warps), leaving the
-// result for column lane cl in part[tw0 * 32 + cl] where tw0 is the team's
-// first warp; visible to the whole team on return.
-// Every thread merges the team's warp partials itself (in warp order, so
-// all of them hold the same bits): two barriers, no serial merge.
+// Merge the row groups of a team (kPipeTeamWarps warps) through `part`,
+// the start of the stage the team holds: warp w's partial for column lane
+// cl goes to part[w * 32 + cl].  The first barrier also means every warp of
+// the team is done reading the stage's rows (and a previous merge's
+// partials) before they are overwritten, so the partials need no shared
+// memory of their own and the stages get it.  Every thread merges the
+// team's warp partials itself (in warp order, so all of them hold the same
+// bits): two barriers, no serial merge.  The caller fences the generic
+// writes against the bulk copy that next fills the stage.
 template <int OP, int VEC>
 __device__ __forceinline__ void team_merge(Acc<OP, VEC> &acc, Acc<OP, VEC> *part, int team, int wit, int q, int cl,
                                            int G) {
   for (int m = 16; m >= G; m >>= 1) acc.shfl_xor_merge(m);
-  const int base = team * kPipeTeamWarps;
-  named_sync(1 + team, 32 * kPipeTeamWarps);  // part[] of the team's previous merge has been read
-  if (q == 0) part[(base + wit) * 32 + cl] = acc;
   named_sync(1 + team, 32 * kPipeTeamWarps);
-  acc = part[base * 32 + cl];
+  if (q == 0) part[wit * 32 + cl] = acc;
+  named_sync(1 + team, 32 * kPipeTeamWarps);
+  acc = part[cl];
 #pragma unroll
-  for (int w = 1; w < kPipeTeamWarps; ++w) acc.merge(part[(base + w) * 32 + cl]);
+  for (int w = 1; w < kPipeTeamWarps; ++w) acc.merge(part[w * 32 + cl]);
 }
 
 // Fold rows held in shared memory: softmax takes its exact-maximum
@@ -125,9 +146,8 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
   constexpr int W = PartialWidth<OP>::value;
   extern __shared__ __align__(128) char smem[];
   char *const stages = smem;
-  Acc<OP, VEC> *const part = reinterpret_cast<Acc<OP, VEC> *>(smem + S * L::kStageBytes);
-  StageRecord *const rec = reinterpret_cast<StageRecord *>(smem + S * L::kStageBytes + L::kPartBytes);
-  uint64_t *const full = reinterpret_cast<uint64_t *>(smem + S * L::kStageBytes + L::kPartBytes + L::kRecordBytes);
+  StageRecord *const rec = reinterpret_cast<StageRecord *>(smem + S * L::kStageBytes);
+  uint64_t *const full = reinterpret_cast<uint64_t *>(smem + S * L::kStageBytes + L::kRecordBytes);
   uint64_t *const empty = full + S;
   int *const last_flag = reinterpret_cast<int *>(empty + S);  // [kPipeTeams]
 
@@ -389,6 +409,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         if (lane == 0) mbar_arrive(&empty[s]);
         continue;
       }
+      Acc<OP, VEC> *const part = reinterpret_cast<Acc<OP, VEC> *>(stages + static_cast<int64_t>(s) * L::kStageBytes);
       Acc<OP, VEC> acc = split_acc;
       team_merge<OP, VEC>(acc, part, team, wit, q, cl, G);
       if (wit == 0 && q == 0 && active) store_partial<OP, VEC>(acc, a.partials + (c * W) * d + col, d);
@@ -430,6 +451,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
           }
         }
       }
+      fence_proxy_async_shared();  // the partials written into the stage, before its next bulk copy
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
