@@ -67,6 +67,18 @@ def _overlaps(left: Any, right: Any) -> bool:
     return lstart < rend and rstart < lend
 
 
+def _check_gathered(gathered, edges, world: int, torch):
+    """The all-gather result a sharded call hands to the combine kernel:
+    every rank's edge record, f32, contiguous, on this rank's device."""
+    if not isinstance(gathered, torch.Tensor) or gathered.device != edges.device:
+        raise ValidationError("exchange must return every rank's edge record on this device")
+    if gathered.dtype != torch.float32 or not gathered.is_contiguous():
+        raise ValidationError("exchange must return a contiguous f32 tensor (the records as sent)")
+    if gathered.numel() != world * edges.numel():
+        raise ValidationError("exchange must return every rank's edge record on this device")
+    return gathered
+
+
 class CompiledProgram:
     def __init__(self, spec: ProgramSpec, artifact: Artifact, *, cache_hit: bool = False,
                  naive: "CompiledProgram | None" = None):
@@ -301,21 +313,12 @@ class CompiledProgram:
             raise ValidationError("need 0 <= rank < world")
         from .sharding import shard_rows
         row0, row1 = shard_rows(total_rows, world, rank, splits)
-        for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
-            if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
-                raise RuntimeUnavailable(f"{name} must be a CUDA tensor; no CPU execution fallback exists")
-            if not tensor.is_contiguous():
-                raise ValidationError(f"{name} must be row-major contiguous")
         d = self.spec.feature_dim
-        b = offsets.numel() - 1
+        b = self._validate_shard_tensors(values, offsets, out, torch)
         if tuple(values.shape) != (row1 - row0, d):
             raise ValidationError(f"values must hold this rank's {row1 - row0} rows: shape ({row1 - row0}, {d})")
         if tuple(out.shape) != (b, d):
             raise ValidationError(f"out shape must be ({b}, {d})")
-        dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype]
-        offset_dtype = {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype]
-        if values.dtype != dtype or out.dtype != dtype or offsets.dtype != offset_dtype:
-            raise ValidationError("tensor dtype differs from compiled dtype/offsets specialization")
         started = time.perf_counter()
         with torch.cuda.device(values.device):
             active = stream if stream is not None else torch.cuda.current_stream(values.device)
@@ -330,9 +333,7 @@ class CompiledProgram:
                                            values.data_ptr() if values.numel() else 0, offsets.data_ptr(),
                                            out.data_ptr(), edges.data_ptr(), scratch.data_ptr(), nbytes, self._flags,
                                            active.cuda_stream, splits)
-                gathered = exchange(edges)
-                if gathered.numel() != world * edges.numel() or gathered.device != values.device:
-                    raise ValidationError("exchange must return every rank's edge record on this device")
+                gathered = _check_gathered(exchange(edges), edges, world, torch)
                 _native.shard_combine(spec.op, spec.dtype, d, world, rank, gathered.data_ptr(), out.data_ptr(),
                                       self._flags, active.cuda_stream)
         result = self._report("rowbalanced", {"sharded": {"world": world, "rank": rank, "rows": [row0, row1]}},
@@ -353,20 +354,11 @@ class CompiledProgram:
             raise ValidationError("need 0 <= rank < world")
         from .sharding import shard_rows
         row0, row1 = shard_rows(total_rows, world, rank, splits)
-        for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
-            if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
-                raise RuntimeUnavailable(f"{name} must be a CUDA tensor; no CPU execution fallback exists")
-            if not tensor.is_contiguous():
-                raise ValidationError(f"{name} must be row-major contiguous")
         d = self.spec.feature_dim
-        b = offsets.numel() - 1
+        b = self._validate_shard_tensors(values, offsets, out, torch)
         rows = (row1 - row0, d)
         if tuple(values.shape) != rows or tuple(out.shape) != rows:
             raise ValidationError(f"values and out must hold this rank's {row1 - row0} rows: shape {rows}")
-        dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype]
-        offset_dtype = {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype]
-        if values.dtype != dtype or out.dtype != dtype or offsets.dtype != offset_dtype:
-            raise ValidationError("tensor dtype differs from compiled dtype/offsets specialization")
         if len(offsets_host) != b + 1:
             raise ValidationError("offsets_host must hold the same B+1 offsets")
         spec = self.spec
@@ -384,9 +376,7 @@ class CompiledProgram:
                 first = _native.run_shard_softmax(spec.dtype, spec.offsets_dtype, d, total_rows, b, world, rank,
                                                   segments, ptr, offsets.data_ptr(), edges.data_ptr(),
                                                   scratch.data_ptr(), nbytes, self._flags, active.cuda_stream, splits)
-                gathered = exchange(edges)
-                if gathered.numel() != world * edges.numel() or gathered.device != values.device:
-                    raise ValidationError("exchange must return every rank's edge record on this device")
+                gathered = _check_gathered(exchange(edges), edges, world, torch)
                 report = _native.shard_softmax_finish(spec.dtype, spec.offsets_dtype, d, total_rows, b, world, rank,
                                                       segments, ptr, offsets.data_ptr(), gathered.data_ptr(),
                                                       out.data_ptr() if out.numel() else 0, scratch.data_ptr(),
@@ -395,6 +385,27 @@ class CompiledProgram:
         result = self._report("rowbalanced", {"sharded": {"world": world, "rank": rank, "rows": [row0, row1],
                                                           "segments": list(segments)}}, started, report, nbytes)
         return replace(result, kernel_names=names + result.kernel_names)
+
+    def _validate_shard_tensors(self, values, offsets, out, torch) -> int:
+        """Tensor checks shared by both sharded paths (the single-GPU rules
+        of ``_validate_tensors`` that do not depend on the rank's window);
+        returns B.  Pointer alignment and overlap are checked by the C ABI."""
+        for name, tensor in (("values", values), ("offsets", offsets), ("out", out)):
+            if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
+                raise RuntimeUnavailable(f"{name} must be a CUDA tensor; no CPU execution fallback exists")
+            if not tensor.is_contiguous():
+                raise ValidationError(f"{name} must be row-major contiguous")
+            if tensor.requires_grad:
+                raise ValidationError("autograd is outside the supported forward-only contract")
+        if values.device != offsets.device or values.device != out.device:
+            raise ValidationError("values, offsets and out must use the same CUDA device")
+        if offsets.ndim != 1 or offsets.numel() < 1:
+            raise ValidationError("offsets must have shape [B+1], including [0] when B=0")
+        dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype]
+        offset_dtype = {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype]
+        if values.dtype != dtype or out.dtype != dtype or offsets.dtype != offset_dtype:
+            raise ValidationError("tensor dtype differs from compiled dtype/offsets specialization")
+        return offsets.numel() - 1
 
     def _report(self, schedule, selection, started, report, nbytes, validation=None) -> ExecutionReport:
         validation, validation_ms = validation if validation is not None else (None, None)

@@ -228,3 +228,30 @@ def test_sharded_softmax_through_the_runtime(cuda):
     torch.cuda.synchronize()
     assert "rowbalanced_normalize" in report.kernel_names
     check(out.cpu().numpy().astype(np.float64), values, offsets, "softmax", "f32")
+
+
+@pytest.mark.parametrize("op", ["sum", "softmax"])
+@pytest.mark.parametrize("problem", ["grad", "gathered-bf16", "gathered-strided", "gathered-short"])
+def test_sharded_runtime_rejects_bad_tensors(cuda, op, problem):
+    """run_sharded refuses autograd inputs and an exchange result that is
+    not every rank's f32 record, contiguous, before the combine launch."""
+    torch = cuda
+    from ragged import ValidationError
+    from helpers import program
+    offsets = np.array([0, 3, 9], dtype=np.int64)
+    values = torch.randn((9, 8), device="cuda")
+    out = torch.full((9 if op == "softmax" else 2, 8), -64.0, device="cuda")
+    exchange = {
+        "gathered-bf16": lambda edges: edges.to(torch.bfloat16),
+        "gathered-strided": lambda edges: torch.stack([edges, edges], 1)[:, 0],
+        "gathered-short": lambda edges: edges[:-1],
+    }.get(problem, lambda edges: edges)
+    if problem == "grad":
+        values.requires_grad_()
+    kwargs = {"offsets_host": offsets} if op == "softmax" else {}
+    with pytest.raises(ValidationError):
+        program(op, "f32", 8, "i64").run_sharded(values, torch.from_numpy(offsets).cuda(), out, total_rows=9, world=1,
+                                                 rank=0, exchange=exchange, **kwargs)
+    torch.cuda.synchronize()
+    if problem == "grad":
+        assert torch.all(out == -64).item()
