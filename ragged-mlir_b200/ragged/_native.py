@@ -30,8 +30,10 @@ MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.
 EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_info", "rg_workspace_bytes",
-            "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_pointwise_workspace_bytes", "rg_run_pointwise", "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes", "rg_shard_segments", "rg_shard_softmax_workspace_bytes", "rg_run_shard_softmax", "rg_shard_softmax_finish",
-            "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
+            "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_pointwise_workspace_bytes", "rg_run_pointwise",
+            "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
+            "rg_shard_segments", "rg_shard_softmax_workspace_bytes", "rg_run_shard_softmax",
+            "rg_shard_softmax_finish", "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
 
 
 class Report(ctypes.Structure):
@@ -210,9 +212,14 @@ def shard_edge_bytes(op: str, d: int) -> int:
     return int(out.value)
 
 
-def _splits_arg(splits):
+def _splits_arg(splits, world: int):
+    """(pointer, owner) of a split's world + 1 row boundaries, or None.  The
+    library reads exactly world + 1 entries, so a list of another length is
+    refused here, before it could read past the array."""
     if splits is None:
         return None
+    if len(splits) != world + 1:
+        raise ValidationError(f"splits must hold world + 1 = {world + 1} row boundaries, not {len(splits)}")
     array = (ctypes.c_int64 * len(splits))(*[int(x) for x in splits])
     return ctypes.cast(array, ctypes.POINTER(ctypes.c_int64)), array
 
@@ -230,7 +237,7 @@ def shard_split(offsets_host, index: str, world: int, end_weight: float) -> list
 def shard_workspace_bytes(op: str, dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int,
                           flags: int = 0, splits=None) -> int:
     out = ctypes.c_int64(0)
-    arg = _splits_arg(splits)
+    arg = _splits_arg(splits, world)
     raise_for(library().rg_shard_workspace_bytes(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank,
                                                  arg[0] if arg else None, flags, ctypes.byref(out)),
               "rg_shard_workspace_bytes")
@@ -241,7 +248,7 @@ def run_shard(op: str, dtype: str, index: str, d: int, n: int, b: int, world: in
               offsets_ptr: int, out_ptr: int, edges_ptr: int, workspace_ptr: int, workspace_bytes: int, flags: int,
               stream: int, splits=None) -> Report:
     report = Report()
-    arg = _splits_arg(splits)
+    arg = _splits_arg(splits, world)
     status = library().rg_run_shard(OPS[op], DTYPES[dtype], INDEX[index], d, n, b, world, rank, arg[0] if arg else None,
                                     values_ptr or None, offsets_ptr, out_ptr, edges_ptr, workspace_ptr or None,
                                     workspace_bytes, flags, stream or None, ctypes.byref(report))
@@ -260,7 +267,7 @@ def shard_segments(offsets_host, index: str, world: int, rank: int, splits=None)
     import numpy as np
     offs = np.ascontiguousarray(offsets_host, dtype=np.int32 if index == "i32" else np.int64)
     seg0, seg1 = ctypes.c_int64(0), ctypes.c_int64(0)
-    arg = _splits_arg(splits)
+    arg = _splits_arg(splits, world)
     raise_for(library().rg_shard_segments(offs.ctypes.data, INDEX[index], offs.size - 1, world, rank,
                                           arg[0] if arg else None, ctypes.byref(seg0), ctypes.byref(seg1)),
               "rg_shard_segments")
@@ -270,7 +277,7 @@ def shard_segments(offsets_host, index: str, world: int, rank: int, splits=None)
 def shard_softmax_workspace_bytes(dtype: str, index: str, d: int, n: int, b: int, world: int, rank: int,
                                   segments: tuple[int, int], flags: int = 0, splits=None) -> int:
     out = ctypes.c_int64(0)
-    arg = _splits_arg(splits)
+    arg = _splits_arg(splits, world)
     raise_for(library().rg_shard_softmax_workspace_bytes(DTYPES[dtype], INDEX[index], d, n, b, world, rank,
                                                          arg[0] if arg else None, segments[0], segments[1], flags,
                                                          ctypes.byref(out)), "rg_shard_softmax_workspace_bytes")
@@ -281,7 +288,7 @@ def run_shard_softmax(dtype: str, index: str, d: int, n: int, b: int, world: int
                       segments: tuple[int, int], values_ptr: int, offsets_ptr: int, edges_ptr: int, workspace_ptr: int,
                       workspace_bytes: int, flags: int, stream: int, splits=None) -> Report:
     report = Report()
-    arg = _splits_arg(splits)
+    arg = _splits_arg(splits, world)
     raise_for(library().rg_run_shard_softmax(DTYPES[dtype], INDEX[index], d, n, b, world, rank,
                                              arg[0] if arg else None, segments[0], segments[1], values_ptr or None,
                                              offsets_ptr, edges_ptr, workspace_ptr or None, workspace_bytes, flags,
@@ -293,7 +300,7 @@ def shard_softmax_finish(dtype: str, index: str, d: int, n: int, b: int, world: 
                          segments: tuple[int, int], values_ptr: int, offsets_ptr: int, gathered_ptr: int, out_ptr: int,
                          workspace_ptr: int, workspace_bytes: int, flags: int, stream: int, splits=None) -> Report:
     report = Report()
-    arg = _splits_arg(splits)
+    arg = _splits_arg(splits, world)
     raise_for(library().rg_shard_softmax_finish(DTYPES[dtype], INDEX[index], d, n, b, world, rank,
                                                 arg[0] if arg else None, segments[0], segments[1],
                                                 values_ptr or None, offsets_ptr, gathered_ptr, out_ptr or None,

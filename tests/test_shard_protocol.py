@@ -327,3 +327,15 @@ def test_shard_segments_cover_every_window_row():
                 for s in range(b):
                     if offsets[s] < row1 and offsets[s + 1] > row0:
                         assert seg0 <= s < seg1, (world, rank, s, seg0, seg1)
+
+
+@pytest.mark.parametrize("splits", [[0, 540], [0, 100, 540], [0, 100, 200, 300, 540], []])
+def test_native_split_arguments_must_hold_world_plus_one_boundaries(splits):
+    """The C ABI reads world + 1 boundaries from a split pointer; the
+    binding refuses a list of another length before calling it."""
+    from ragged import ValidationError, _native
+    offsets = offsets_of(np.array([40, 0, 500], dtype=np.int64))
+    with pytest.raises(ValidationError, match="world \\+ 1"):
+        _native.shard_segments(offsets, "i64", 3, 1, splits)
+    with pytest.raises(ValidationError, match="world \\+ 1"):
+        _native.shard_workspace_bytes("sum", "f32", "i64", 4, 540, 3, 3, 1, 0, splits)
