@@ -170,6 +170,9 @@ int rg_check_offsets(int index_dtype, int64_t n, int64_t b, const void *offsets,
  * rank) and calls rg_shard_combine, which writes the cut segments this rank
  * finishes.  Together the ranks write every output row exactly once (each
  * on the rank that holds the segment's end).  Sum and max only.
+ * Every `splits` argument below is NULL (the even row split) or HOST memory
+ * holding exactly world + 1 nondecreasing row boundaries from 0 to n: the
+ * library reads world + 1 entries and cannot check the array's length.
  * The reference is single-GPU; these entry points are this build's
  * multi-GPU extension of its launcher (runtime/Driver.h:21-54). */
 
