@@ -230,6 +230,29 @@ def test_sharded_softmax_through_the_runtime(cuda):
     check(out.cpu().numpy().astype(np.float64), values, offsets, "softmax", "f32")
 
 
+@pytest.mark.parametrize("op", ["sum", "max"])
+def test_sharded_reduction_through_the_runtime(cuda, op):
+    """CompiledProgram.run_sharded for sum and max (the path bench.py takes
+    on several GPUs) on one rank of a world of one, with an explicit even
+    split: the exchange is the identity and every output row is this
+    rank's."""
+    torch = cuda
+    from helpers import program
+    lengths = make_lengths("long_tail", 400, 60_000, seed=94)
+    lengths[::13] = 0
+    offsets = offsets_of(lengths)
+    n = int(offsets[-1])
+    values = prepared(np.random.default_rng(95).normal(size=(n, 64)), "bf16")
+    dv = torch.from_numpy(values).cuda().to(torch.bfloat16)
+    out = torch.full((offsets.size - 1, 64), SENTINEL, dtype=torch.bfloat16, device="cuda")
+    report = program(op, "bf16", 64, "i64").run_sharded(dv, torch.from_numpy(offsets).cuda(), out, total_rows=n,
+                                                         world=1, rank=0, exchange=lambda edges: edges,
+                                                         splits=[0, n])
+    torch.cuda.synchronize()
+    assert report.kernel_names[0].startswith("rowbalanced")
+    check(out.float().cpu().numpy().astype(np.float64), values, offsets, op, "bf16")
+
+
 @pytest.mark.parametrize("op", ["sum", "softmax"])
 @pytest.mark.parametrize("problem", ["grad", "gathered-bf16", "gathered-strided", "gathered-short"])
 def test_sharded_runtime_rejects_bad_tensors(cuda, op, problem):
