@@ -58,10 +58,8 @@ struct ClsState {
   unsigned long long cta_count;    // CTA-class segments
   unsigned long long split_packed; // (chunks << 28) | split segments
   unsigned long long work;         // next work item of the worker
-  unsigned long long norm_work;    // unused (kept for the state layout)
   unsigned long long error;        // nonzero: a bounded wait gave up
   unsigned long long split_work;   // next split chunk of the pipelined worker
-  unsigned long long pad;
 };
 
 // Chunk length of a split segment of `len` rows: the item length, or longer
