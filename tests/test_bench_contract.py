@@ -1,0 +1,62 @@
+"""bench.py's reference arm on the host (no GPU): the JSON line the round
+driver parses, and the rule that only rank 0 of a multi-rank launch runs it.
+The arm times the float64 C oracle (the reference's CPU implementation of
+the path), so it runs here; the GPU arm is covered by the GPU tests.
+"""
+from __future__ import annotations
+
+import json
+import os
+from pathlib import Path
+import subprocess
+import sys
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def run_bench(*args: str, env: dict | None = None) -> subprocess.CompletedProcess:
+    full_env = {**os.environ, **(env or {})}
+    return subprocess.run([sys.executable, str(REPO / "bench.py"), *args], cwd=REPO, env=full_env,
+                          capture_output=True, text=True, timeout=300)
+
+
+@pytest.fixture(scope="module")
+def reference_line():
+    # 200 steps bound the oracle's timing to about one second.
+    result = run_bench("--impl", "reference", "--workload", "c1", "--scale", "0.01", "--steps", "200",
+                       "--warmup", "3")
+    assert result.returncode == 0, result.stderr[-2000:]
+    lines = [line for line in result.stdout.splitlines() if line.strip()]
+    assert len(lines) == 1, result.stdout
+    return json.loads(lines[0])
+
+
+def test_reference_line_has_every_contract_key(reference_line):
+    line = reference_line
+    assert line["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["value"] > 0 and line["unit"] == "GB/s" and line["higher_is_better"] is True
+    assert (line["n_gpus"], line["steps"], line["warmup"]) == (1, 200, 3)
+    assert line["config"]["workload"] == "c1" and line["data"] == "synthetic"
+    assert set(line["cpu_baseline"]) == {"value", "unit", "cores", "kind", "sample"}
+    assert line["cpu_baseline"]["value"] == line["value"] and line["cpu_baseline"]["kind"] == "port"
+    assert line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_reference_metric_matches_the_gpu_arm(reference_line):
+    sys.path.insert(0, str(REPO))
+    import bench
+    assert reference_line["metric"] == bench.metric_name()
+
+
+def test_only_rank_zero_runs_the_reference_arm():
+    result = run_bench("--impl", "reference", "--workload", "c1", "--scale", "0.01", "--gpus", "2", "--steps",
+                       "200", "--warmup", "3", env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
+    assert result.returncode == 0, result.stderr[-2000:]
+    assert result.stdout.strip() == ""
