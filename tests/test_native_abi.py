@@ -51,3 +51,29 @@ def test_argument_errors_need_no_device(native_library):
     # i32 offsets with N beyond the i32 range.
     status = native_library.rg_run(0, 0, 0, 4, 2**31, 1, None, None, None, None, 0, 1, -1, 0, None, None)
     assert status == _native.RG_ERR_INVALID_ARGUMENT
+
+
+def test_missing_library_raises_instead_of_falling_back(monkeypatch, tmp_path):
+    """Without libragged_b200.so the package refuses to run: there is no
+    CPU implementation to fall back on."""
+    import pytest
+    from ragged import RuntimeUnavailable, _native
+    monkeypatch.setattr(_native, "_lib", None)
+    with pytest.raises(RuntimeUnavailable, match="no CPU fallback"):
+        _native.library(tmp_path / "libragged_b200.so")
+
+
+def test_host_tensors_are_refused_not_computed(native_library, tmp_path):
+    """run() and run_sharded() with tensors in host memory raise
+    RuntimeUnavailable before any launch; nothing is computed on the CPU."""
+    import pytest
+    torch = pytest.importorskip("torch")
+    from ragged import ArtifactCache, Compiler, ProgramSpec, RuntimeUnavailable
+    program = Compiler().compile(ProgramSpec("sum", "f32", 4, "i64"), ArtifactCache(tmp_path))
+    values, offsets = torch.ones((6, 4)), torch.tensor([0, 2, 6])
+    out = torch.full((2, 4), -1.0)
+    with pytest.raises(RuntimeUnavailable, match="no CPU execution fallback"):
+        program.run(values, offsets, out)
+    with pytest.raises(RuntimeUnavailable, match="no CPU execution fallback"):
+        program.run_sharded(values, offsets, out, total_rows=6, world=1, rank=0, exchange=lambda edges: edges)
+    assert torch.all(out == -1).item()
