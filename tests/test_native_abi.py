@@ -77,3 +77,19 @@ def test_host_tensors_are_refused_not_computed(native_library, tmp_path):
     with pytest.raises(RuntimeUnavailable, match="no CPU execution fallback"):
         program.run_sharded(values, offsets, out, total_rows=6, world=1, rank=0, exchange=lambda edges: edges)
     assert torch.all(out == -1).item()
+
+
+def test_exchange_result_checks():
+    """The all-gather result handed to the combine kernel must be every
+    rank's f32 record, contiguous, on the records' device (host logic)."""
+    import pytest
+    torch = pytest.importorskip("torch")
+    from ragged import ValidationError
+    from ragged.runtime import _check_gathered
+    edges = torch.zeros(16)
+    good = torch.zeros(48)
+    assert _check_gathered(good, edges, 3, torch) is good
+    for bad in (torch.zeros(47), torch.zeros(48, dtype=torch.bfloat16), torch.zeros(96)[::2],
+                torch.zeros(48).numpy()):
+        with pytest.raises(ValidationError):
+            _check_gathered(bad, edges, 3, torch)
