@@ -873,7 +873,11 @@ shard_softmax_combine_kernel(float *__restrict__ stats, int64_t d, int vec_cols,
 // floats).  Rank `rank` owns the segment of its head piece if it consumed
 // that segment's end; the pieces merge in rank order: the starting rank's
 // tail piece, the head pieces of ranks the segment passes through, then
-// this rank's head piece.  One CTA per column tile.
+// this rank's head piece.  A rank whose window holds no rows (a split with
+// repeated boundaries) records no piece: header (-1, 0, -1).  Such a record
+// can only sit inside the segment's chain, because a rank with rows inside
+// an open segment always records it, so the walk back steps over it and its
+// (unwritten) pieces are never read.  One CTA per column tile.
 template <typename T, int OP, int VEC>
 __global__ void __launch_bounds__(32)
 shard_combine_kernel(T *__restrict__ out, int64_t d, int vec_cols, int world, int rank,
@@ -887,21 +891,23 @@ shard_combine_kernel(T *__restrict__ out, int64_t d, int vec_cols, int world, in
   const int cv = blockIdx.y * 32 + threadIdx.x;
   if (cv >= vec_cols) return;
   const int64_t col = static_cast<int64_t>(cv) * VEC;
-  int k = rank - 1;  // walk back over ranks the segment passes through
-  while (k > 0) {
-    const int64_t *h = reinterpret_cast<const int64_t *>(gathered + k * rec);
-    if (h[0] == seg && h[1] == 0) --k;
+  auto header = [&](int k) { return reinterpret_cast<const int64_t *>(gathered + k * rec); };
+  auto empty = [&](const int64_t *h) { return h[0] < 0 && h[2] < 0; };
+  int k = rank - 1;  // walk back over ranks the segment passes through (or that hold no rows)
+  while (k >= 0) {
+    const int64_t *h = header(k);
+    if ((h[0] == seg && h[1] == 0) || empty(h)) --k;
     else break;
   }
   Acc total;
   total.init();
   if (k >= 0) {
-    const int64_t *h = reinterpret_cast<const int64_t *>(gathered + k * rec);
-    if (h[2] == seg) total.merge_piece(gathered + k * rec + kEdgeHeader + wd + col, d);            // tail piece
-    else if (h[0] == seg) total.merge_piece(gathered + k * rec + kEdgeHeader + col, d);            // rank 0 through
+    const int64_t *h = header(k);
+    if (h[2] == seg) total.merge_piece(gathered + k * rec + kEdgeHeader + wd + col, d);  // the starting rank's tail
   }
-  for (int j = k + 1; j < rank; ++j) total.merge_piece(gathered + j * rec + kEdgeHeader + col, d);  // through ranks
-  total.merge_piece(gathered + rank * rec + kEdgeHeader + col, d);                                 // this rank's head
+  for (int j = k + 1; j < rank; ++j)  // ranks the segment passes through (their head pieces)
+    if (header(j)[0] == seg) total.merge_piece(gathered + j * rec + kEdgeHeader + col, d);
+  total.merge_piece(gathered + rank * rec + kEdgeHeader + col, d);  // this rank's head
   float y[VEC];
   total.value(y);
   VecIO<T, VEC>::store(out + seg * d + col, y);

@@ -278,3 +278,33 @@ def test_sharded_runtime_rejects_bad_tensors(cuda, op, problem):
     torch.cuda.synchronize()
     if problem == "grad":
         assert torch.all(out == -64).item()
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("splits", [[0, 1, 2, 2, 3, 3, 3, 3, 3], [0, 1, 1, 1, 2, 2, 3, 3, 3], "balanced"])
+def test_sharded_ranks_without_rows_inside_a_segment(cuda, op, splits):
+    """Repeated split boundaries leave ranks with no rows while a segment is
+    open across them: their edge records hold no piece, and the rank that
+    finishes the segment must still merge the starting rank's tail piece.
+    The balanced split of one 3-row segment over 8 ranks makes such a split."""
+    from ragged.sharding import balanced_split
+    offsets = np.array([0, 3], dtype=np.int64)
+    values = prepared(np.array([[1.5, -2.0, 4.0], [0.25, 8.0, -1.0], [3.0, 0.5, 2.0]]), "f32")
+    if splits == "balanced":
+        splits = balanced_split(offsets, 8)
+        assert len(set(splits)) < len(splits), "expected repeated boundaries"
+    actual = run_world(cuda, op, "f32", values, offsets, 8, list(splits))
+    check(actual, values, offsets, op, "f32")
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+def test_sharded_empty_ranks_inside_a_giant_segment(cuda, op):
+    """A long segment with ranks of no rows between the ranks holding it, and
+    short segments around it, bf16 D=256 (the c5 row shape)."""
+    lengths = np.array([5, 20_000, 0, 7, 3000, 1], dtype=np.int64)
+    offsets = offsets_of(lengths)
+    n = int(offsets[-1])
+    splits = [0, 3000, 9000, 9000, 9000, 15000, 20003, 20003, n]
+    values = prepared(np.random.default_rng(44).normal(size=(n, 256)), "bf16")
+    actual = run_world(cuda, op, "bf16", values, offsets, 8, splits)
+    check(actual, values, offsets, op, "bf16")

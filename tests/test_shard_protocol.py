@@ -78,29 +78,35 @@ def combine(op, records, rank, d):
     head_seg, head_ends = int(records[rank][0]), int(records[rank][1])
     if head_seg < 0 or head_ends == 0:
         return None
+    def passes(j):  # the segment runs through rank j, or rank j holds no rows (records nothing)
+        through = int(records[j][0]) == head_seg and int(records[j][1]) == 0
+        return through or (int(records[j][0]) < 0 and int(records[j][2]) < 0)
+
     k = rank - 1
-    while k > 0 and int(records[k][0]) == head_seg and int(records[k][1]) == 0:
+    while k >= 0 and passes(k):
         k -= 1
     head = lambda j: records[j][HEADER:HEADER + d]
     tail = lambda j: records[j][HEADER + d:]
-    total = tail(k) if int(records[k][2]) == head_seg else head(k)
+    ident = np.zeros(d) if op == "sum" else np.full(d, -np.inf)
+    total = tail(k) if k >= 0 and int(records[k][2]) == head_seg else ident
     for j in range(k + 1, rank):
-        total = _merge(op, total, head(j))
+        if int(records[j][0]) == head_seg:
+            total = _merge(op, total, head(j))
     return head_seg, _merge(op, total, head(rank))
 
 
 def _worker(rank, world, port, cases, results):
     import torch
     import torch.distributed as dist
-    from ragged.sharding import balanced_split, shard_rows
+    from ragged.sharding import shard_rows
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         out = []
-        for op, values, offsets, balanced in cases:
+        for op, values, offsets, split in cases:
             n = int(offsets[-1])
-            splits = balanced_split(offsets, world) if balanced else None
+            splits = _split_of(split, offsets, world)
             row0, row1 = shard_rows(n, world, rank, splits)
             finished, record = rank_part(op, values[row0:row1], offsets, row0, row1, rank)
             mine = torch.from_numpy(record)
@@ -135,20 +141,40 @@ def _cases():
         values[10, 1] = np.nan
         cases.append((op, values, offsets))
         cases.append((op, rng.normal(size=(2, 2)), np.array([0, 0, 2, 2], dtype=np.int64)))  # more ranks than rows
-    return [(op, values, offsets, balanced) for op, values, offsets in cases for balanced in (False, True)]
+    out = [(op, values, offsets, split) for op, values, offsets in cases for split in (None, "balanced")]
+    # Ranks with no rows inside one segment: repeated split boundaries (given
+    # explicitly, and as the balanced split of a 3-row segment makes them).
+    for op in ("sum", "max"):
+        values = rng.normal(size=(3, 2))
+        out.append((op, values, np.array([0, 3], dtype=np.int64), "repeat"))
+        out.append((op, values, np.array([0, 3], dtype=np.int64), "balanced"))
+        out.append((op, rng.normal(size=(5, 2)), np.array([0, 1, 4, 4, 5], dtype=np.int64), "repeat"))
+    return out
+
+
+def _split_of(split, offsets, world):
+    """None (even rows), "balanced" or "repeat": every rank but the last gets
+    at most one row and repeated boundaries leave ranks without rows."""
+    from ragged.sharding import balanced_split
+    if split == "balanced":
+        return balanced_split(offsets, world)
+    if split == "repeat":
+        n = int(offsets[-1])
+        return [0] + [min(n, (k + 1) // 2) for k in range(1, world)] + [n]
+    return None
 
 
 @pytest.mark.parametrize("world", [2, 3])
 def test_sharding_protocol_over_gloo(world):
     import torch.multiprocessing as mp
     from oracle import reference_port as rp
-    from ragged.sharding import balanced_split, segment_owners
+    from ragged.sharding import segment_owners
     cases = _cases()
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.start_processes(_worker, args=(world, _free_port(), cases, results), nprocs=world, start_method="spawn")
-    for i, (op, values, offsets, balanced) in enumerate(cases):
-        owners = segment_owners(offsets, world, balanced_split(offsets, world) if balanced else None)
+    for i, (op, values, offsets, split) in enumerate(cases):
+        owners = segment_owners(offsets, world, _split_of(split, offsets, world))
         seen = {}
         for rank in range(world):
             for s, row in results[rank][i].items():
@@ -261,15 +287,15 @@ def finish_softmax(values_local, offsets, row0, row1, rank, stats, records):
 def _softmax_worker(rank, world, port, cases, results):
     import torch
     import torch.distributed as dist
-    from ragged.sharding import balanced_split, shard_rows
+    from ragged.sharding import shard_rows
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         out = []
-        for values, offsets, balanced in cases:
+        for values, offsets, split in cases:
             n = int(offsets[-1])
-            splits = balanced_split(offsets, world) if balanced else None
+            splits = _split_of(split, offsets, world)
             row0, row1 = shard_rows(n, world, rank, splits)
             local = values[row0:row1]
             stats, record = rank_part_softmax(local, offsets, row0, row1, rank)
@@ -297,12 +323,13 @@ def test_sharded_softmax_protocol_over_gloo(world):
     values[10, 1] = np.nan
     values[1200:1300, 2] = -np.inf
     cases.append((values, offsets))
-    cases = [(v, o, balanced) for v, o in cases for balanced in (False, True)]
+    cases = [(v, o, split) for v, o in cases for split in (None, "balanced")]
+    cases += [(rng.normal(size=(3, 2)), np.array([0, 3], dtype=np.int64), split) for split in ("repeat", "balanced")]
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.start_processes(_softmax_worker, args=(world, _free_port(), cases, results), nprocs=world, start_method="spawn")
     for i, (values, offsets, _) in enumerate(cases):
-        parts = sorted(results[rank][i] for rank in range(world))
+        parts = sorted((results[rank][i] for rank in range(world)), key=lambda part: (part[0], part[1].shape[0]))
         actual = np.concatenate([p[1] for p in parts], axis=0)
         with np.errstate(all="ignore"):
             expected = rp.segment_softmax(values, offsets)
