@@ -1,189 +1,184 @@
-"""Content-addressed artifact records (the reference's python/ragged/cache.py).
+"""Program records bound to one build of the native library.
 
-On B200 every kernel is built into libragged_b200.so, so an artifact is no
-longer a cubin: it is a manifest binding one ``ProgramSpec`` to the exact
-library build (its sha256 and version) that runs it.  The reference's cache
-contract is kept -- ``ArtifactCache(root).load(key)`` / ``.publish(...)``,
-immutable entries published atomically (fsync + rename under a
-per-signature lock), ``CacheMiss`` / ``CacheMismatch`` /
-``SpecializationLimit`` -- so that ``Compiler(...).compile(spec, cache)``
-keeps its meaning: a second compile of the same spec against the same
-library is a cache hit, and a library rebuilt underneath a cache is a
-mismatch rather than a silent reuse.
+The reference's ``ArtifactCache`` (python/ragged/cache.py) stored one cubin
+per specialization.  Here every kernel is compiled into libragged_b200.so
+once, so what ``Compiler.compile`` has to remember about a ``ProgramSpec``
+is small: which schedules it may run, recorded against the exact library
+build that runs them.  ``ArtifactCache(root)`` keeps those records in one
+JSON ledger per library build:
+
+    <root>/ledger-<first 16 hex digits of the library sha256>.json
+        {"format": 2, "library_sha256": ..., "library_version": ...,
+         "records": {<spec ir_hash>: {"key": ..., "metadata": ..., "check": ...}}}
+
+* A record is looked up by the spec's ``ir_hash``; ``check`` is the SHA256
+  of the record's canonical JSON (key and metadata), so a record edited on
+  disk is refused with ``CacheMismatch`` rather than trusted, and so is a
+  ledger whose header names another library build.
+* A rebuilt library gets a new ledger: records never outlive the build they
+  describe.
+* Writers take an exclusive ``flock`` on ``<ledger>.lock``, re-read the
+  ledger, add their record and replace the file atomically (temporary file,
+  fsync, ``os.replace``): readers see the old or the new ledger, never a
+  partial one, and concurrent compilers do not lose each other's records.
+* At most ``max_specializations`` records share a signature
+  (op:dtype:D:offsets:chip); one more raises ``SpecializationLimit``.
 """
 from __future__ import annotations
 
-from contextlib import contextmanager
 from dataclasses import asdict, dataclass
 import fcntl
 import hashlib
 import json
 import os
 from pathlib import Path
-import shutil
 import tempfile
-from typing import Any, Iterator
+from typing import Any
 
-from .errors import CacheError, CacheMismatch, CacheMiss, SpecializationLimit, ValidationError
+from .errors import CacheMismatch, CacheMiss, SpecializationLimit, ValidationError
 from .model import DIALECT_VERSION, ProgramSpec, canonical_json
 
-
-def _sha(data: bytes) -> str:
-    return hashlib.sha256(data).hexdigest()
+LEDGER_FORMAT = 2
 
 
-def _unique_object(pairs):
-    result = {}
-    for key, value in pairs:
-        if key in result:
-            raise ValueError(f"duplicate manifest field: {key}")
-        result[key] = value
-    return result
+def _sha256(text: str) -> str:
+    return hashlib.sha256(text.encode()).hexdigest()
 
 
-def _hex64(value: Any) -> bool:
+def _is_digest(value: Any) -> bool:
     return isinstance(value, str) and len(value) == 64 and all(c in "0123456789abcdef" for c in value)
 
 
 @dataclass(frozen=True)
 class CacheKey:
+    """What a program record is bound to: the specialization (its IR hash and
+    signature) and the library build (version and sha256)."""
+
     ir_hash: str
-    dialect_version: str
+    signature: str
     library_version: str
     library_sha256: str
-    chip: str
-    strategy: str
-    dtype: str
-    feature_dim: int
-    offsets_dtype: str
-    op: str
+    dialect_version: str = DIALECT_VERSION
 
     def __post_init__(self) -> None:
-        if not _hex64(self.ir_hash):
-            raise ValidationError("ir_hash must be a SHA256 hex digest")
-        if not _hex64(self.library_sha256):
-            raise ValidationError("library_sha256 must be a SHA256 hex digest")
-        for name in ("dialect_version", "library_version"):
-            value = getattr(self, name)
-            if not isinstance(value, str) or not value.strip():
-                raise ValidationError(f"cache key requires a nonempty {name}")
-        ProgramSpec(self.op, self.dtype, self.feature_dim, self.offsets_dtype, strategy=self.strategy, chip=self.chip)
+        if not _is_digest(self.ir_hash) or not _is_digest(self.library_sha256):
+            raise ValidationError("a cache key needs SHA256 hex digests for the spec and the library")
+        if not isinstance(self.library_version, str) or not self.library_version.strip():
+            raise ValidationError("a cache key needs the library version")
 
     @classmethod
-    def from_spec(cls, spec: ProgramSpec, *, library_version: str, library_sha256: str,
-                  dialect_version: str = DIALECT_VERSION) -> "CacheKey":
-        return cls(spec.ir_hash, dialect_version, library_version, library_sha256, spec.chip, spec.strategy,
-                   spec.dtype, spec.feature_dim, spec.offsets_dtype, spec.op)
+    def from_spec(cls, spec: ProgramSpec, *, library_version: str, library_sha256: str) -> "CacheKey":
+        if not isinstance(spec, ProgramSpec):
+            raise ValidationError("spec must be a ProgramSpec")
+        return cls(spec.ir_hash, spec.signature, library_version, library_sha256)
 
     def to_dict(self) -> dict[str, Any]:
         return asdict(self)
 
     @property
     def digest(self) -> str:
-        return _sha(canonical_json(self.to_dict()).encode())
-
-    @property
-    def signature(self) -> str:
-        return f"{self.op}:{self.dtype}:D{self.feature_dim}:{self.offsets_dtype}:{self.chip}"
+        """Identity of the (specialization, library build) pair."""
+        return _sha256(canonical_json(self.to_dict()))
 
 
 @dataclass(frozen=True)
 class Artifact:
+    """One program record: its key, its metadata and the ledger holding it."""
+
     path: Path
     key: CacheKey
     metadata: dict[str, Any]
 
 
-class ArtifactCache:
-    """Per-signature directories of immutable manifest entries."""
+def _record_check(key: dict, metadata: dict) -> str:
+    return _sha256(canonical_json({"key": key, "metadata": metadata}))
 
-    SCHEMA = 1
+
+class ArtifactCache:
+    """JSON ledgers of program records, one per library build (see module doc)."""
+
     MAX_SPECIALIZATIONS = 16
 
     def __init__(self, root: str | os.PathLike[str], *, max_specializations: int | None = None):
         self.root = Path(root).expanduser()
+        self.max_specializations = self.MAX_SPECIALIZATIONS
         if max_specializations is not None:
             if type(max_specializations) is not int or max_specializations < 1:
                 raise ValidationError("max_specializations must be a positive integer")
-            self.MAX_SPECIALIZATIONS = max_specializations
+            self.max_specializations = max_specializations
 
-    def _signature_dir(self, key: CacheKey) -> Path:
-        return self.root / _sha(key.signature.encode())
+    def ledger_path(self, key: CacheKey) -> Path:
+        return self.root / f"ledger-{key.library_sha256[:16]}.json"
 
-    def entry_path(self, key: CacheKey) -> Path:
-        return self._signature_dir(key) / key.digest
+    def _read(self, key: CacheKey) -> dict:
+        path = self.ledger_path(key)
+        try:
+            ledger = json.loads(path.read_text(encoding="utf-8"))
+        except FileNotFoundError:
+            return {"format": LEDGER_FORMAT, "library_sha256": key.library_sha256,
+                    "library_version": key.library_version, "records": {}}
+        except (OSError, ValueError) as exc:
+            raise CacheMismatch(f"unreadable cache ledger {path}: {exc}") from exc
+        if not isinstance(ledger, dict) or ledger.get("format") != LEDGER_FORMAT or \
+                not isinstance(ledger.get("records"), dict):
+            raise CacheMismatch(f"cache ledger {path} has an unknown format")
+        if ledger.get("library_sha256") != key.library_sha256:
+            raise CacheMismatch(f"cache ledger {path} belongs to another library build")
+        return ledger
 
-    @contextmanager
-    def _locked(self, key: CacheKey) -> Iterator[Path]:
-        directory = self._signature_dir(key)
-        directory.mkdir(parents=True, exist_ok=True)
-        with (directory / ".publish.lock").open("a+b") as lock:
-            fcntl.flock(lock, fcntl.LOCK_EX)
-            try:
-                yield directory
-            finally:
-                fcntl.flock(lock, fcntl.LOCK_UN)
+    def _artifact(self, key: CacheKey, record: Any) -> Artifact:
+        if not isinstance(record, dict) or set(record) != {"key", "metadata", "check"}:
+            raise CacheMismatch("cache record fields differ from this build's format")
+        if canonical_json(record["key"]) != canonical_json(key.to_dict()):
+            raise CacheMismatch("cache record key differs from the requested specialization and library")
+        if not isinstance(record["metadata"], dict):
+            raise CacheMismatch("cache record metadata must be an object")
+        if record["check"] != _record_check(record["key"], record["metadata"]):
+            raise CacheMismatch("cache record content does not match its SHA256 check")
+        return Artifact(self.ledger_path(key), key, record["metadata"])
 
     def load(self, key: CacheKey) -> Artifact:
-        path = self.entry_path(key)
-        if not path.exists():
-            raise CacheMiss(f"no artifact for {key.digest}")
-        try:
-            if path.is_symlink() or not path.is_dir():
-                raise CacheMismatch(f"cache entry must be a directory: {path}")
-            if (path / "manifest.json").is_symlink():
-                raise CacheMismatch("cache manifest must not be a symbolic link")
-            manifest = json.loads((path / "manifest.json").read_text(encoding="utf-8"), object_pairs_hook=_unique_object)
-            expected = {"schema", "key", "cache_key", "signature", "metadata", "metadata_sha256"}
-            if not isinstance(manifest, dict) or set(manifest) != expected:
-                raise CacheMismatch("cache manifest schema fields differ")
-            if manifest["schema"] != self.SCHEMA:
-                raise CacheMismatch("cache manifest schema version differs")
-            if canonical_json(manifest["key"]) != canonical_json(key.to_dict()):
-                raise CacheMismatch("cache manifest key differs from the requested library/target key")
-            if manifest["cache_key"] != key.digest or manifest["signature"] != key.signature:
-                raise CacheMismatch("cache manifest digest or signature differs")
-            if not isinstance(manifest["metadata"], dict):
-                raise CacheMismatch("cache metadata must be an object")
-            if _sha(canonical_json(manifest["metadata"]).encode()) != manifest["metadata_sha256"]:
-                raise CacheMismatch("artifact metadata does not match manifest SHA256")
-            return Artifact(path, key, manifest["metadata"])
-        except CacheError:
-            raise
-        except (OSError, ValueError, TypeError, KeyError) as exc:
-            raise CacheMismatch(f"incomplete or invalid cache entry {path}: {exc}") from exc
+        """The record of ``key``; ``CacheMiss`` when there is none."""
+        record = self._read(key)["records"].get(key.ir_hash)
+        if record is None:
+            raise CacheMiss(f"no program record for {key.signature} ({key.ir_hash[:12]})")
+        return self._artifact(key, record)
 
     def publish(self, key: CacheKey, metadata: dict[str, Any]) -> Artifact:
+        """Add the record of ``key`` (idempotent for identical metadata)."""
         if not isinstance(metadata, dict):
-            raise ValidationError("artifact metadata must be a dictionary")
+            raise ValidationError("program metadata must be a dictionary")
         metadata = json.loads(canonical_json(metadata))
-        manifest = {"schema": self.SCHEMA, "key": key.to_dict(), "cache_key": key.digest,
-                    "signature": key.signature, "metadata": metadata,
-                    "metadata_sha256": _sha(canonical_json(metadata).encode())}
-        with self._locked(key) as directory:
-            destination = self.entry_path(key)
-            if destination.exists():
-                artifact = self.load(key)
-                if artifact.metadata != metadata:
-                    raise CacheMismatch("refusing to replace immutable artifact with different content")
-                return artifact
-            entries = [p for p in directory.iterdir() if not p.name.startswith(".")]
-            if len(entries) >= self.MAX_SPECIALIZATIONS:
-                raise SpecializationLimit(
-                    f"signature {key.signature} already has {self.MAX_SPECIALIZATIONS} specializations")
-            temporary = Path(tempfile.mkdtemp(prefix=".pending-", dir=directory))
+        self.root.mkdir(parents=True, exist_ok=True)
+        path = self.ledger_path(key)
+        with open(path.with_suffix(".lock"), "a+b") as lock:
+            fcntl.flock(lock, fcntl.LOCK_EX)
             try:
-                with (temporary / "manifest.json").open("xb") as stream:
-                    stream.write((canonical_json(manifest) + "\n").encode())
-                    stream.flush()
-                    os.fsync(stream.fileno())
-                os.rename(temporary, destination)
-                fd = os.open(directory, os.O_RDONLY | os.O_DIRECTORY)
+                ledger = self._read(key)
+                records = ledger["records"]
+                existing = records.get(key.ir_hash)
+                if existing is not None:
+                    artifact = self._artifact(key, existing)
+                    if artifact.metadata != metadata:
+                        raise CacheMismatch("a program record exists with different metadata")
+                    return artifact
+                same = sum(1 for r in records.values()
+                           if isinstance(r, dict) and r.get("key", {}).get("signature") == key.signature)
+                if same >= self.max_specializations:
+                    raise SpecializationLimit(f"signature {key.signature} already has {same} specializations")
+                records[key.ir_hash] = {"key": key.to_dict(), "metadata": metadata,
+                                        "check": _record_check(key.to_dict(), metadata)}
+                handle, temporary = tempfile.mkstemp(prefix=".ledger-", dir=self.root)
                 try:
-                    os.fsync(fd)
-                finally:
-                    os.close(fd)
+                    with os.fdopen(handle, "w", encoding="utf-8") as stream:
+                        stream.write(canonical_json(ledger) + "\n")
+                        stream.flush()
+                        os.fsync(stream.fileno())
+                    os.replace(temporary, path)
+                except BaseException:
+                    if os.path.exists(temporary):
+                        os.unlink(temporary)
+                    raise
             finally:
-                if temporary.exists():
-                    shutil.rmtree(temporary)
+                fcntl.flock(lock, fcntl.LOCK_UN)
         return self.load(key)

@@ -7,6 +7,7 @@ test_selection.py) for this build.
 from __future__ import annotations
 
 import json
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -85,13 +86,36 @@ def test_cache_rejects_tampering_and_limits(tmp_path, native_library):
     Compiler().compile(ProgramSpec("sum", "f32", 8, hints=Hints(max_len=3), strategy="naive"), cache)
     with pytest.raises(SpecializationLimit):
         Compiler().compile(ProgramSpec("sum", "f32", 8, hints=Hints(max_len=4), strategy="naive"), cache)
-    entry = next(p for p in tmp_path.rglob("manifest.json"))
-    manifest = json.loads(entry.read_text())
-    manifest["metadata"]["schedules"] = ["rowbalanced"]
-    entry.write_text(json.dumps(manifest))
+    ledger_path = next(tmp_path.glob("ledger-*.json"))
+    ledger = json.loads(ledger_path.read_text())
+    for record in ledger["records"].values():
+        record["metadata"]["schedules"] = ["rowbalanced"]
+    ledger_path.write_text(json.dumps(ledger))
     with pytest.raises(CacheMismatch, match="SHA256"):
-        for max_len in (None, 3):
-            Compiler().compile(ProgramSpec("sum", "f32", 8, hints=Hints(max_len=max_len), strategy="naive"), cache)
+        Compiler().compile(ProgramSpec("sum", "f32", 8, hints=Hints(max_len=3), strategy="naive"), cache)
+    ledger["library_sha256"] = "0" * 64
+    ledger_path.write_text(json.dumps(ledger))
+    with pytest.raises(CacheMismatch, match="another library build"):
+        Compiler().compile(ProgramSpec("sum", "f32", 8, strategy="naive"), cache)
+
+
+def test_cache_ledger_survives_concurrent_publishers(tmp_path, native_library):
+    """Processes publishing different specializations into one ledger at
+    once: every record lands (the flock + re-read + atomic replace)."""
+    import multiprocessing
+    context = multiprocessing.get_context("spawn")
+    with context.Pool(4) as pool:
+        pool.starmap(_publish_one, [(str(tmp_path), d) for d in range(1, 13)])
+    cache = ArtifactCache(tmp_path)
+    for d in range(1, 13):
+        assert Compiler().compile(ProgramSpec("max", "f32", d, strategy="naive"), cache).cache_hit
+
+
+def _publish_one(root, d):
+    import sys
+    sys.path[:0] = [str(Path(__file__).resolve().parents[1] / "ragged-mlir_b200")]
+    from ragged import ArtifactCache as Cache, Compiler as Comp, ProgramSpec as Spec
+    Comp().compile(Spec("max", "f32", d, strategy="naive"), Cache(root))
 
 
 def test_schedules_for():

@@ -125,7 +125,7 @@ def test_mode_reaches_the_registered_program(monkeypatch, kind):
     program = SimpleNamespace(spec=ProgramSpec(kind, feature_dim=4),
                               artifact=SimpleNamespace(key=SimpleNamespace(digest="mode-routing-" + kind)),
                               run=lambda values, offsets, out, **kwargs: calls.append(kwargs))
-    monkeypatch.setattr(torch_adapter, "_programs", {})
+    monkeypatch.setattr(torch_adapter, "_table", torch_adapter.ProgramTable())
     values, offsets = torch.empty((6, 4)), torch.tensor([0, 2, 6])
     if kind == "softmax":
         output = torch_adapter.segment_softmax(values, offsets, program=program, mode="checked")
@@ -142,7 +142,7 @@ def test_bind_routes_through_the_custom_op(monkeypatch):
     program = SimpleNamespace(spec=ProgramSpec("sum", feature_dim=4),
                               artifact=SimpleNamespace(key=SimpleNamespace(digest="bind-routing")),
                               run=lambda values, offsets, out, **kwargs: calls.append((out.shape, kwargs)))
-    monkeypatch.setattr(torch_adapter, "_programs", {})
+    monkeypatch.setattr(torch_adapter, "_table", torch_adapter.ProgramTable())
     execute = torch_adapter.bind(program)
     assert execute(torch.empty((6, 4)), torch.tensor([0, 2, 6])).shape == (2, 4)
     assert calls == [((2, 4), {"mode": "validated"})]
@@ -199,7 +199,7 @@ def test_njt_mask_routes_the_dense_mask(monkeypatch):
     program = SimpleNamespace(spec=ProgramSpec("softmax", feature_dim=4, mask=True),
                               artifact=SimpleNamespace(key=SimpleNamespace(digest="njt-mask-routing")),
                               run=lambda values, offsets, out, **kwargs: calls.append(kwargs))
-    monkeypatch.setattr(torch_adapter, "_programs", {})
+    monkeypatch.setattr(torch_adapter, "_table", torch_adapter.ProgramTable())
     values, offsets, mask = torch.empty((6, 4)), torch.tensor([0, 2, 6]), torch.empty((6, 4))
     out = torch_adapter.njt_softmax(torch.nested.nested_tensor_from_jagged(values, offsets), program=program,
                                     mode="checked", mask=mask)
