@@ -1,29 +1,40 @@
 """Benchmark: segmented reduction throughput on B200 (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c5] [--schedule auto] [--no-e2e] [--configs]
+                    [--workload c5] [--schedule auto] [--no-e2e] [--no-configs]
 
 A step is one pass of the hot path over one batch: one segmented reduction
 of the whole workload (default ``c5``: bf16 sum, D=256, N=200M rows, B=4M
 Zipf segments -- the configuration the metric is quoted on at 1/2/4/8
 GPUs).  With N GPUs (torchrun, one process per GPU) the rows are split
-evenly across ranks (strong scaling: the total work is fixed), each rank
+across ranks by work (strong scaling: the total work is fixed), each rank
 reduces its rows, and the partial sums of segments cut by shard boundaries
 are combined over NVLink (NCCL all-gather + a deterministic combine kernel).
+
+Before anything is timed, the first call's output is checked against the
+float64 C oracle (``"parity": "ok"`` in the line; a mismatch exits
+non-zero): at N=1 the leading segments, the three 50M-row segments and the
+last segments; at N>1 the same segments, each rank reducing its own rows of
+them in the oracle and rank 0 merging the pieces in rank order and
+comparing the rows their owners wrote.
 
 value          = algorithmic bytes of the whole job / max-over-ranks device
                  time per step (GB/s), inputs resident in HBM;
 e2e            = the same metric through the public API with the inputs in
                  pinned host memory: H2D copy, the call, D2H of the result,
                  every step inside the timed region;
-roofline       = the dominant kernel's achieved bandwidth vs the measured
-                 copy bandwidth in MEASURED_PEAKS.json;
-cpu_baseline   = the CPU oracle port (C, float64, all host threads) on a
-                 bounded sample of the same workload (rank 0, N=1 only).
+roofline       = the call's achieved bandwidth per GPU vs the measured copy
+                 bandwidth in MEASURED_PEAKS.json;
+configs        = (N=1) c1-c4 of the configuration list, each checked against
+                 the oracle at full size and timed the same way;
+cpu_baseline   = the reference's CPU path on the host's cores (all of its
+                 CPU affinity): torch.segment_reduce (softmax: the CPU torch
+                 composition) and the float64 C oracle on a bounded sample
+                 of the same workload (rank 0, N=1 only); the faster is the
+                 line's value.
 
-``--impl reference`` times the reference's CPU implementation of the path
-(the oracle port; the reference's own GPU path cannot run on sm_100) on the
-host cores and prints its line with "impl": "reference".
+``--impl reference`` times that CPU path (the reference's GPU path cannot
+run on sm_100) and prints its line with "impl": "reference".
 """
 from __future__ import annotations
 
@@ -51,9 +62,10 @@ PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 # profiles/rowbal_kernel_c5.md.
 TRAFFIC_RATIO = {"c5": 1.003}
 FALLBACK_HBM_GBS = 6650.0
+SIDE_CONFIGS = ("c1", "c2_sum", "c2_max", "c3", "c4_sum", "c4_max")
 
 
-def parse_args():
+def parse_args(argv=None):
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=10)
@@ -64,9 +76,11 @@ def parse_args():
     parser.add_argument("--scale", type=float, default=1.0, help="shrink B and N (testing only)")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--configs", action="store_true", help="also time c1-c4 on one GPU (extra key)")
-    parser.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline work")
-    return parser.parse_args()
+    parser.add_argument("--no-configs", action="store_true", help="skip the c1-c4 entries (N=1)")
+    parser.add_argument("--no-parity", action="store_true", help="skip the oracle check of the first call")
+    parser.add_argument("--cpu-bytes", type=float, default=2e9,
+                        help="algorithmic bytes of the CPU sample (one call of each CPU implementation)")
+    return parser.parse_args(argv)
 
 
 def peak_hbm() -> tuple[float, str]:
@@ -75,6 +89,26 @@ def peak_hbm() -> tuple[float, str]:
         return float(data["hbm_gbs"]), "measured"
     except (OSError, ValueError, KeyError):
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def host_threads() -> int:
+    """Host threads this process may use: its CPU affinity (torchrun sets
+    OMP_NUM_THREADS=1, which must not shrink the CPU baseline)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
+
+
+def metric_name() -> str:
+    return "effective HBM GB/s of segmented reduction (algorithmic bytes / device time per call)"
+
+
+def config_dict(w, args, flush) -> dict:
+    return {"workload": w.name, "op": w.op, "values_dtype": w.dtype, "accumulate": "f32", "D": w.d, "N": w.n,
+            "B": w.b, "offsets": w.index, "schedule": args.schedule, "algorithmic_bytes": w.algorithmic_bytes(),
+            "parallelism": f"row-sharded x{args.gpus}", "l2": flush, **({"lengths_rule": w.notes["lengths_rule"]}
+                                                                      if "lengths_rule" in w.notes else {})}
 
 
 # --------------------------------------------------------------- clocks ----
@@ -89,6 +123,7 @@ class ClockSampler:
     def __init__(self, device: int):
         self.device = device
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
         try:
@@ -115,7 +150,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, sm_max, reasons, power = [], 0.0, set(), []
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in getattr(self, "lines", []):
+        for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -135,82 +170,102 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
-# ------------------------------------------------------------ workload ----
+# ----------------------------------------------------------- CPU legs ----
 
-def device_values(torch, w, rows: tuple[int, int], device) -> "torch.Tensor":
-    """Values of rows [lo, hi) generated on the device (deterministic per
-    row chunk, so every rank builds exactly its slice of one dataset)."""
-    lo, hi = rows
-    tdtype = torch.float32 if w.dtype == "f32" else torch.bfloat16
-    out = torch.empty((hi - lo, w.d), dtype=tdtype, device=device)
-    chunk = 1 << 22  # rows per generator chunk
-    first = lo // chunk
-    for c in range(first, (hi + chunk - 1) // chunk):
-        a, b = max(lo, c * chunk), min(hi, (c + 1) * chunk)
-        g = torch.Generator(device=device)
-        g.manual_seed(1_000_003 * w.value_seed + c)
-        block = torch.empty(((c + 1) * chunk - c * chunk, w.d), dtype=tdtype, device=device)
-        if w.value_kind == "uniform":
-            block.uniform_(-1.0, 1.0, generator=g)
-        else:
-            block.normal_(0.0, 2.0 if w.value_kind == "normal2" else 1.0, generator=g)
-        if w.nan_fraction or w.neginf_fraction:
-            u = torch.rand(block.shape, generator=g, device=device)
-            block[u < w.nan_fraction] = float("nan")
-            block[(u >= w.nan_fraction) & (u < w.nan_fraction + w.neginf_fraction)] = float("-inf")
-            del u
-        out[a - lo:b - lo] = block[a - c * chunk:b - c * chunk]
-        del block
-    return out
-
-
-def flush_l2(torch, buffer):
-    buffer.add_(1)  # writes 2x the L2 (read + write of a buffer > L2)
-
-
-# ------------------------------------------------------------- CPU leg ----
-
-def cpu_sample(w, seconds: float):
-    """(values f32/bf16-as-f32 host array, offsets, bytes) of a leading,
-    segment-aligned sample of the workload sized for about ``seconds`` of
-    multi-threaded oracle work at a conservative 2 GB/s."""
-    target_bytes = int(seconds * 2e9 / 4)  # one call ~ a quarter of the budget
-    row_bytes = w.d * w.element_bytes
-    target_rows = max(1, min(w.n, target_bytes // row_bytes))
+def cpu_sample(w, target_bytes: float):
+    """A leading, segment-aligned sample of the workload of about
+    ``target_bytes`` algorithmic bytes: (bf16/f32 host tensor, offsets,
+    rows), values drawn on the host by torch's generator (same
+    distribution as the device data)."""
+    import torch
+    row_bytes = w.d * w.element_bytes * (2 if w.op == "softmax" else 1)
+    target_rows = max(1, min(w.n, int(target_bytes // row_bytes)))
     offsets = w.offsets().astype(np.int64)
-    last = int(np.searchsorted(offsets, target_rows, side="right")) - 1
-    last = max(1, last)
+    last = max(1, int(np.searchsorted(offsets, target_rows, side="right")) - 1)
+    if int(offsets[last]) == 0:
+        last = min(w.b, 1 + int(np.argmax(offsets[1:] > 0)))
     sample_offsets = offsets[:last + 1].copy()
     rows = int(sample_offsets[-1])
-    if rows == 0:
-        last = min(w.b, 1 + int(np.argmax(offsets[1:] > 0)))
-        sample_offsets = offsets[:last + 1].copy()
-        rows = int(sample_offsets[-1])
-    values = w.host_values(slice(0, rows))
+    values = workloads.device_values(w, (0, rows), torch.device("cpu"))
     index = np.int32 if w.index == "i32" else np.int64
     return values, sample_offsets.astype(index), rows
 
 
-def run_cpu_baseline(w, seconds: float) -> dict:
-    from oracle import native as coracle  # CPU baseline leg only
-    values, offsets, rows = cpu_sample(w, seconds)
-    threads = coracle.max_threads()
+def _torch_softmax(torch, values, offsets):
+    """The reference's CPU torch softmax: segment max, exp, segment sum,
+    divide, in f32 (bf16 promoted first and the result cast back)."""
+    work = values.float()
+    lengths = offsets[1:] - offsets[:-1]
+    ids = torch.repeat_interleave(torch.arange(lengths.numel()), lengths)
+    maxima = torch.segment_reduce(work, "max", offsets=offsets, axis=0)
+    weights = torch.exp(work - maxima[ids])
+    totals = torch.segment_reduce(weights, "sum", offsets=offsets, axis=0)
+    return (weights / totals[ids]).to(values.dtype)
+
+
+def cpu_legs(w, target_bytes: float, timed_calls: int, warmup: int, threads: int) -> dict:
+    """Both CPU implementations of the path on one bounded sample: the
+    reference's torch baseline (baselines/torch_reference.py:12-16 of the
+    reference: bf16 promoted to f32, torch.segment_reduce, cast back;
+    softmax the CPU torch composition) with torch.set_num_threads(all), and
+    the float64 C oracle on the same threads.  The faster one, by its
+    median over ``timed_calls`` calls after ``warmup``, is the baseline;
+    the other is timed on 3 calls."""
+    import torch
+    from oracle import native as coracle  # the CPU baseline leg
+    torch.set_num_threads(threads)
+    values, offsets, rows = cpu_sample(w, target_bytes)
     b = offsets.size - 1
     s_off = 4 if offsets.dtype == np.int32 else 8
     rows_out = rows if w.op == "softmax" else b
     nbytes = rows * w.d * w.element_bytes + (b + 1) * s_off + rows_out * w.d * w.element_bytes
-    coracle.run(w.op, values, offsets, dtype=w.dtype, threads=threads)  # warm-up
-    times = []
-    deadline = time.perf_counter() + seconds
-    while time.perf_counter() < deadline or len(times) < 2:
+    toff = torch.from_numpy(offsets.astype(np.int64))
+    raw = values.view(torch.int16).numpy().view(np.uint16) if w.dtype == "bf16" else values.numpy()
+
+    def torch_call():
+        if w.op == "softmax":
+            return _torch_softmax(torch, values, toff)
+        work = values.float() if w.dtype == "bf16" else values
+        return torch.segment_reduce(work, w.op, offsets=toff, axis=0).to(values.dtype)
+
+    def oracle_call():
+        return coracle.run(w.op, raw, offsets, dtype=w.dtype, threads=threads)
+
+    legs = {"torch": torch_call, "oracle": oracle_call}
+    probe = {}
+    for name, call in legs.items():
+        call()  # first touch of the sample and of the thread pool
         t0 = time.perf_counter()
-        coracle.run(w.op, values, offsets, dtype=w.dtype, threads=threads)
-        times.append(time.perf_counter() - t0)
-    best = statistics.median(times)
-    return {"value": round(nbytes / best / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"leading {rows} rows / {b} segments of {w.name} ({nbytes / 1e9:.2f} GB algorithmic), "
-                      f"float64 C oracle, median of {len(times)} calls",
-            "seconds_per_call": round(best, 4)}
+        call()
+        probe[name] = time.perf_counter() - t0
+    fast = min(probe, key=probe.get)
+    results = {}
+    for name, call in legs.items():
+        calls = timed_calls if name == fast else 3
+        for _ in range(max(0, (warmup if name == fast else 1) - 1)):
+            call()
+        times = []
+        for _ in range(calls):
+            t0 = time.perf_counter()
+            call()
+            times.append(time.perf_counter() - t0)
+        per_call = statistics.median(times)
+        results[name] = {"value": round(nbytes / per_call / 1e9, 4), "unit": "GB/s",
+                         "seconds_per_call": round(per_call, 5), "calls": calls,
+                         "dtype": "f32" if name == "torch" else "f64"}
+    what = {"torch": "torch.segment_reduce on CPU (f32)" if w.op != "softmax" else
+            "CPU torch segment max / exp / segment sum / divide (f32)",
+            "oracle": "float64 C oracle (restated oracle/reference.py)"}
+    sample = (f"leading {rows} rows / {b} segments of {w.name} ({nbytes / 1e9:.3f} GB algorithmic) on "
+              f"{threads} host threads")
+    return {"fast": fast, "legs": results, "what": what, "sample": sample, "cores": threads, "bytes": nbytes}
+
+
+def cpu_baseline_entry(legs: dict) -> dict:
+    fast = legs["fast"]
+    return {"value": legs["legs"][fast]["value"], "unit": "GB/s", "cores": legs["cores"], "kind": "port",
+            "sample": f"{legs['sample']}; {legs['what'][fast]} (faster of the two), median of "
+                      f"{legs['legs'][fast]['calls']} calls"}
 
 
 def reference_arm(args) -> None:
@@ -218,47 +273,48 @@ def reference_arm(args) -> None:
     if rank != 0:
         return
     w = workloads.make(args.workload, scale=args.scale)
-    # Each step is one bounded sample call; the run is sized to a few minutes.
-    per_step = max(1.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
-    base = run_cpu_baseline(w, per_step)
-    line = {"impl": "reference", "metric": metric_name(), "value": base["value"], "unit": "GB/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(base["seconds_per_call"] * 1000, 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": config_dict(w, args, "n/a"),
-            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "the reference's GPU path is sm_86/sm_89 MLIR cubins and cannot load on sm_100; its CPU "
-                    "implementation of the path (the float64 oracle, restated in C and run on all host threads) "
-                    "is timed instead"}
+    threads = host_threads()
+    legs = cpu_legs(w, args.cpu_bytes, args.steps, args.warmup, threads)
+    fast = legs["legs"][legs["fast"]]
+    base = cpu_baseline_entry(legs)
+    line = {"impl": "reference", "metric": metric_name(), "value": fast["value"], "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": fast["calls"], "warmup": args.warmup,
+            "ms_per_step": round(fast["seconds_per_call"] * 1000, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": fast["dtype"], "data": "synthetic",
+            "config": config_dict(w, args, "n/a (host)"),
+            "cpu_baseline": base,
+            "e2e": {"value": fast["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "legs": {name: {**leg, "impl": legs["what"][name]} for name, leg in legs["legs"].items()},
+            "note": "the reference's GPU path is sm_86/sm_89 MLIR cubins and cannot load on sm_100; its CPU path "
+                    "is timed instead, each step one call on a bounded sample of the workload (ms_per_step is per "
+                    "sample call)"}
     print(json.dumps(line), flush=True)
 
 
-def metric_name() -> str:
-    return "effective HBM GB/s of segmented reduction (algorithmic bytes / device time per call)"
+# ------------------------------------------------------------ timing ----
 
+def flush_l2(buffer):
+    buffer.add_(1)  # writes 2x the L2 (read + write of a buffer > L2)
 
-def config_dict(w, args, flush) -> dict:
-    return {"workload": w.name, "op": w.op, "values_dtype": w.dtype, "accumulate": "f32", "D": w.d, "N": w.n,
-            "B": w.b, "offsets": w.index, "schedule": args.schedule, "algorithmic_bytes": w.algorithmic_bytes(),
-            "parallelism": f"row-sharded x{args.gpus}", "l2": flush, **({"lengths_rule": w.notes["lengths_rule"]}
-                                                                      if "lengths_rule" in w.notes else {})}
-
-
-# ---------------------------------------------------------------- ours ----
 
 def time_calls(torch, fn, steps, warmup, stream, flush=None, dist=None):
     """Per-step device time (ms) with CUDA events on ``stream``, the K steps
     bracketed by a barrier and a synchronize on both sides; with ``dist``
-    the per-step times are the maximum over ranks."""
+    the per-step times are the maximum over ranks, and the ranks' streams
+    are aligned by a one-element all-reduce right before the first start
+    event (a host barrier returns at different times on different ranks,
+    and the first collective of the step would charge that skew to step 1)."""
     for _ in range(warmup):
         if flush is not None:
             flush()
         fn()
     torch.cuda.synchronize()
+    align = None
     if dist is not None:
+        align = torch.zeros(1, device=torch.device("cuda", torch.cuda.current_device()))
         dist.barrier()
         torch.cuda.synchronize()
+        dist.all_reduce(align)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
@@ -286,6 +342,97 @@ def time_calls(torch, fn, steps, warmup, stream, flush=None, dist=None):
 RANK_MS: list = []  # mean step time of every rank in the last multi-GPU timing
 
 
+# ------------------------------------------------------------ parity ----
+
+def fetcher(torch, tensor):
+    """``fetch(lo, hi)`` for the oracle checker: rows of a device tensor as
+    the host array the C oracle reads (f32, or bf16 as raw uint16 bits)."""
+    def fetch(lo, hi):
+        block = tensor[lo:hi]
+        if block.dtype == torch.bfloat16:
+            return block.view(torch.int16).cpu().numpy().view(np.uint16)
+        return block.float().cpu().numpy()
+    return fetch
+
+
+def host_rows(torch, out, segments=None) -> np.ndarray:
+    if segments is None:
+        return out.float().cpu().numpy().astype(np.float64)
+    index = torch.from_numpy(np.asarray(segments, dtype=np.int64)).to(out.device)
+    return out.index_select(0, index).float().cpu().numpy().astype(np.float64)
+
+
+def parity_segments(offsets_host: np.ndarray, lead_rows: int = 2_000_000, tail: int = 2048) -> np.ndarray:
+    """Segments checked on the benchmark's first call: the leading ones up
+    to ``lead_rows`` rows, every segment of at least 1M rows (the giant
+    segments cut across virtual CTAs and ranks) and the last ``tail``."""
+    offsets = np.asarray(offsets_host, dtype=np.int64)
+    b = offsets.size - 1
+    lengths = np.diff(offsets)
+    lead = int(np.searchsorted(offsets, lead_rows, side="right"))
+    picked = np.concatenate([np.arange(min(b, max(1, lead))), np.nonzero(lengths >= 1_000_000)[0],
+                             np.arange(max(0, b - tail), b)])
+    return np.unique(picked)
+
+
+def parity_single(torch, w, values, out, offsets_host) -> dict:
+    """The first call's output (one GPU) against the oracle."""
+    from oracle import device_check as dc  # the checker
+    if w.op == "softmax":
+        dc.check_softmax(host_rows(torch, out), fetcher(torch, values)(0, w.n), offsets_host, dtype=w.dtype)
+        return {"parity": "ok", "parity_rows": w.n}
+    whole = w.n * w.d * w.element_bytes <= 4e9  # c1-c4: every segment; c5: a sample with the giants
+    segments = np.arange(w.b) if whole else parity_segments(offsets_host)
+    dc.check_reduction(host_rows(torch, out, segments), fetcher(torch, values), w.n, offsets_host, segments,
+                       op=w.op, dtype=w.dtype)
+    rows = int(np.sum(np.diff(offsets_host.astype(np.int64))[segments]))
+    return {"parity": "ok", "parity_segments": int(segments.size), "parity_rows": rows}
+
+
+def parity_sharded(torch, dist, w, values, out, offsets_host, row0, rank, world, owners) -> dict:
+    """The first call's output over all ranks: each rank reduces its rows of
+    the checked segments in the oracle; rank 0 merges the float64 pieces in
+    rank order (the oracle's own merge) and compares the rows the owners
+    wrote.  Every rank takes the same collectives; the verdict is shared."""
+    from oracle import device_check as dc, native  # the checker
+    segments = parity_segments(offsets_host)
+    kinds = (w.op, "abssum") if w.op == "sum" else (w.op,)
+    parts = dc.segment_partials(fetcher(torch, values), values.shape[0], w.d, offsets_host, segments, kinds=kinds,
+                                dtype=w.dtype, row_base=row0)
+    device = values.device
+    mine = torch.from_numpy(np.stack(parts)).to(device)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    rows_mine = out.index_select(0, torch.from_numpy(segments).to(device)).float()
+    rows_every = [torch.empty_like(rows_mine) for _ in range(world)]
+    dist.all_gather(rows_every, rows_mine)
+    verdict = torch.zeros(1, dtype=torch.int32, device=device)
+    message = ""
+    if rank == 0:
+        pieces = [e.cpu().numpy() for e in every]
+        merged = pieces[0].copy()
+        for piece in pieces[1:]:
+            for k, kind in enumerate(kinds):
+                merged[k] = native.merge(kind, merged[k], piece[k])
+        owner = owners[segments]
+        gathered = np.stack([r.cpu().numpy() for r in rows_every]).astype(np.float64)
+        actual = gathered[owner, np.arange(segments.size)]
+        lengths = np.diff(offsets_host.astype(np.int64))[segments]
+        try:
+            native.check(actual, w.op, w.dtype, np.concatenate([[0], np.cumsum(lengths)]), merged[0],
+                         merged[1] if w.op == "sum" else None)
+        except AssertionError as exc:
+            verdict.fill_(1)
+            message = str(exc)
+    dist.all_reduce(verdict, op=dist.ReduceOp.MAX)
+    if int(verdict.item()):
+        raise SystemExit(f"parity check of the first call failed: {message or 'see rank 0'}")
+    rows = int(np.sum(np.diff(offsets_host.astype(np.int64))[segments]))
+    return {"parity": "ok", "parity_segments": int(segments.size), "parity_rows": rows}
+
+
+# ---------------------------------------------------------------- ours ----
+
 def ours(args) -> None:
     import torch
     from ragged import ArtifactCache, Compiler, ProgramSpec
@@ -305,31 +452,28 @@ def ours(args) -> None:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     w = workloads.make(args.workload, scale=args.scale)
     if world > 1 and w.op == "softmax":
-        raise SystemExit("sharded calls compute sum and max; run softmax workloads with --gpus 1")
+        raise SystemExit("the benchmark's sharded calls compute sum and max; run softmax workloads with --gpus 1")
     offsets_host = w.offsets()
     splits = balanced_split(offsets_host, world, END_WEIGHT) if world > 1 else None
     rows = shard_rows(w.n, world, rank, splits)
-    values = device_values(torch, w, rows, device)
+    values = workloads.device_values(w, rows, device)
     offsets = torch.from_numpy(offsets_host).to(device)
-    tdtype = values.dtype
     rows_out = w.n if w.op == "softmax" else w.b
-    out = torch.empty((rows_out, w.d), dtype=tdtype, device=device)
-    spec = ProgramSpec(w.op, w.dtype, w.d, w.index)
+    out = torch.empty((rows_out, w.d), dtype=values.dtype, device=device)
     cache = ArtifactCache(REPO / "_build" / "bench-cache", max_specializations=64)
-    program = Compiler().compile(spec, cache)
+    program = Compiler().compile(ProgramSpec(w.op, w.dtype, w.d, w.index), cache)
     max_len = int(w.lengths.max()) if w.b else 0
     select = args.schedule
     stream = torch.cuda.current_stream(device)
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
-    input_bytes = values.numel() * values.element_size()
-    flush_buffer = None
-    flush_note = "inputs larger than L2 (no flush)"
-    if input_bytes < 4 * l2:
+    flush_buffer, flush_note = None, "inputs larger than L2 (no flush)"
+    if values.numel() * values.element_size() < 4 * l2:
         flush_buffer = torch.empty(2 * l2 // 4, dtype=torch.float32, device=device)
         flush_note = "L2 flushed between steps (2x L2 buffer rewritten)"
-
+    flush = (lambda: flush_l2(flush_buffer)) if flush_buffer is not None else None
     report_holder = {}
     exchange = torch_exchange() if world > 1 else None
+    owners = segment_owners(offsets_host, world, splits) if w.op != "softmax" else None
 
     def step():
         if world > 1:
@@ -338,7 +482,15 @@ def ours(args) -> None:
         else:
             report_holder["r"] = program.run(values, offsets, out, select=select, max_len=max_len)
 
-    flush = (lambda: flush_l2(torch, flush_buffer)) if flush_buffer is not None else None
+    # Parity gate: the first call, checked before anything is timed.
+    parity = {"parity": "skipped"}
+    step()
+    torch.cuda.synchronize()
+    if not args.no_parity:
+        if world > 1:
+            parity = parity_sharded(torch, dist, w, values, out, offsets_host, rows[0], rank, world, owners)
+        elif rank == 0:
+            parity = parity_single(torch, w, values, out, offsets_host)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -354,7 +506,7 @@ def ours(args) -> None:
     line = {"metric": metric_name(), "value": round(value, 2), "unit": "GB/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config_dict(w, args, flush_note), "schedule_selected": report.selected,
+            "config": config_dict(w, args, flush_note), **parity, "schedule_selected": report.selected,
             "kernels": list(report.kernel_names) + (["shard_combine"] if world > 1 else []),
             "gpu_launches": launches,
             "step_times_ms": [round(t, 4) for t in times],
@@ -374,17 +526,64 @@ def ours(args) -> None:
                             "collective": "NCCL all-gather of edge records",
                             "edge_bytes_per_rank": _native_edge_bytes(w)}
     if not args.no_e2e:
-        owners = segment_owners(offsets_host, world, splits) if w.op != "softmax" else None
         line["e2e"] = e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream, dist,
                               splits, owners, rank, world, exchange)
+    if world == 1 and not args.no_configs:
+        del values, out, flush_buffer
+        torch.cuda.empty_cache()
+        line["configs"] = side_configs(torch, args, device, stream, cache, peak)
     if not args.no_cpu_baseline and rank == 0 and world == 1:
-        line["cpu_baseline"] = {k: v for k, v in run_cpu_baseline(w, args.cpu_seconds).items()
-                                if k != "seconds_per_call"}
+        legs = cpu_legs(w, args.cpu_bytes, 3, 1, host_threads())
+        line["cpu_baseline"] = cpu_baseline_entry(legs)
+        line["cpu_legs"] = {name: {**leg, "impl": legs["what"][name]} for name, leg in legs["legs"].items()}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def side_configs(torch, args, device, stream, cache, peak) -> dict:
+    """c1-c4 on one GPU: each at full size, its first call checked against
+    the oracle (whole output), then K calls timed like the main workload
+    (L2 flushed between steps when the inputs are smaller than 4x L2)."""
+    from ragged import Compiler, ProgramSpec
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    flush_buffer = torch.empty(2 * l2 // 4, dtype=torch.float32, device=device)
+    entries = {}
+    for name in SIDE_CONFIGS:
+        w = workloads.make(name, scale=args.scale)
+        values = workloads.device_values(w, (0, w.n), device)
+        offsets_host = w.offsets()
+        offsets = torch.from_numpy(offsets_host).to(device)
+        out = torch.empty((w.n if w.op == "softmax" else w.b, w.d), dtype=values.dtype, device=device)
+        program = Compiler().compile(ProgramSpec(w.op, w.dtype, w.d, w.index), cache)
+        max_len = int(w.lengths.max()) if w.b else 0
+        holder = {}
+
+        def call():
+            holder["r"] = program.run(values, offsets, out, max_len=max_len)
+
+        call()
+        torch.cuda.synchronize()
+        parity = parity_single(torch, w, values, out, offsets_host)["parity"] if not args.no_parity else "skipped"
+        small = values.numel() * values.element_size() < 4 * l2
+        with ClockSampler(device.index or 0) as clocks:
+            times = time_calls(torch, call, args.steps, args.warmup, stream,
+                               (lambda: flush_l2(flush_buffer)) if small else None)
+        ms = statistics.median(times)
+        gbs = w.algorithmic_bytes() / (ms / 1e3) / 1e9
+        report = holder["r"]
+        entries[name] = {"op": w.op, "dtype": w.dtype, "D": w.d, "N": w.n, "B": w.b, "offsets": w.index,
+                         "us_per_call": round(ms * 1000, 2), "value": round(gbs, 1), "unit": "GB/s",
+                         "roofline_frac": round(gbs / peak, 4), "schedule_selected": report.selected,
+                         "kernels": list(report.kernel_names), "parity": parity,
+                         "l2": "flushed between steps" if small else "inputs larger than L2",
+                         "target": "0.70 of peak (D >= 64)" if w.d >= 64 else "none (D < 64)",
+                         "clocks": clocks.summary()}
+        del values, out, offsets
+        torch.cuda.empty_cache()
+    return entries
 
 
 def _native_edge_bytes(w) -> int:

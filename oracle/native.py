@@ -18,7 +18,7 @@ HERE = Path(__file__).resolve().parent
 SOURCE = HERE / "segred_oracle.c"
 LIBRARY = HERE / "_build" / "libsegred_oracle.so"
 
-OPS = {"sum": 0, "max": 1, "softmax": 2}
+OPS = {"sum": 0, "max": 1, "softmax": 2, "abssum": 3}
 DTYPES = {"f32": 0, "bf16": 1}
 INDEX = {"i32": 0, "i64": 1}
 
@@ -53,7 +53,13 @@ def _load():
 
 
 def max_threads() -> int:
-    return int(_load().so_max_threads())
+    """Host threads this process may run on (its CPU affinity), independent
+    of OMP_NUM_THREADS (which torchrun sets to 1): the count is passed to
+    every call explicitly."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
 
 
 def _prepare(values: np.ndarray, dtype: str, offsets: np.ndarray):
@@ -75,7 +81,8 @@ def _prepare(values: np.ndarray, dtype: str, offsets: np.ndarray):
 
 def segment_reduce(values: np.ndarray, offsets: np.ndarray, kind: str, *, dtype: str = "f32",
                    threads: int | None = None) -> np.ndarray:
-    """Float64 [B, D] sum or max; ``values`` is [N, D] f32 (or bf16 bits/values)."""
+    """Float64 [B, D] sum, max or sum of |x| (``kind`` "abssum": the scale of
+    the sum tolerance); ``values`` is [N, D] f32 (or bf16 bits/values)."""
     raw, offsets, index = _prepare(values, dtype, offsets)
     n, d = raw.shape
     b = offsets.size - 1
@@ -106,3 +113,23 @@ def run(op: str, values: np.ndarray, offsets: np.ndarray, *, dtype: str = "f32",
     if op == "softmax":
         return segment_softmax(values, offsets, dtype=dtype, threads=threads)
     return segment_reduce(values, offsets, op, dtype=dtype, threads=threads)
+
+
+def merge(kind: str, into: np.ndarray, piece: np.ndarray) -> np.ndarray:
+    """Merge two float64 partial results of the same segments (rows of one
+    segment split in two): the oracle's own cross-thread merge."""
+    if kind == "max":
+        return np.maximum(into, piece)  # np.maximum propagates NaN
+    return into + piece
+
+
+def check(actual: np.ndarray, op: str, dtype: str, offsets: np.ndarray, reference: np.ndarray,
+          scale: np.ndarray | None = None) -> None:
+    """Both tolerance contracts (the reference's ``assert_matches`` and
+    ``check_strict``) for a result whose float64 oracle answer, and for sums
+    the per-segment sum of |x|, were computed here (large inputs: no float64
+    copy of the values is ever made)."""
+    from . import reference_port as rp
+    with np.errstate(all="ignore"):
+        rp.assert_matches(actual, None, offsets, operation=op, input_dtype=dtype, reference=reference, scale=scale)
+        rp.check_strict(actual, None, offsets, operation=op, input_dtype=dtype, reference=reference, scale=scale)

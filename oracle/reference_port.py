@@ -230,10 +230,13 @@ REFERENCES = {"sum": segment_sum, "max": segment_max, "softmax": segment_softmax
 
 def assert_matches(actual: np.ndarray, values: np.ndarray, offsets: np.ndarray, *,
                    operation: str, input_dtype: str,
-                   reference: np.ndarray | None = None) -> dict[str, float | int]:
+                   reference: np.ndarray | None = None,
+                   scale: np.ndarray | None = None) -> dict[str, float | int]:
     """The reference's accuracy contract (``oracle/reference.py:109-174``).
 
-    ``reference`` may pass a precomputed float64 answer for these inputs.
+    ``reference`` may pass a precomputed float64 answer for these inputs and,
+    for sums, ``scale`` the precomputed per-segment sum of |x| (then
+    ``values`` is not read).
     """
     if operation not in REFERENCES:
         raise ValueError("operation must be sum, max, or softmax")
@@ -244,7 +247,10 @@ def assert_matches(actual: np.ndarray, values: np.ndarray, offsets: np.ndarray, 
     expected = _expected(reference, input_dtype)
     actual = np.asarray(actual, dtype=np.float64)
     _compare_nonfinite(actual, expected)
-    scale = segment_sum(np.abs(values), offsets) if operation == "sum" else np.abs(expected)
+    if operation != "sum":
+        scale = np.abs(expected)
+    elif scale is None:
+        scale = segment_sum(np.abs(values), offsets)
     rtol, atol = TOLERANCES[input_dtype]
     finite = np.isfinite(expected)
     error = np.abs(actual[finite] - expected[finite])
@@ -291,7 +297,8 @@ def bf16_ulp(x: np.ndarray) -> np.ndarray:
 
 def check_strict(actual: np.ndarray, values: np.ndarray, offsets: np.ndarray, *,
                  operation: str, input_dtype: str,
-                 reference: np.ndarray | None = None) -> dict[str, float]:
+                 reference: np.ndarray | None = None,
+                 scale: np.ndarray | None = None) -> dict[str, float]:
     """This build's stricter contract, on top of the reference's.
 
     * max: bit-exact values in the output dtype (the round-to-nearest-even
@@ -319,7 +326,8 @@ def check_strict(actual: np.ndarray, values: np.ndarray, offsets: np.ndarray, *,
             raise AssertionError(f"max is not bit-exact at {int(np.sum(~exact))} positions")
         return {"max_abs_error": 0.0}
     if operation == "sum":
-        scale = segment_sum(np.abs(values), offsets)
+        if scale is None:
+            scale = segment_sum(np.abs(values), offsets)
     else:
         scale = None
     if input_dtype == "f32":

@@ -7,6 +7,8 @@
  *   sum      oracle/reference.py:78-79   (np.sum in float64; +0 for an empty segment)
  *   max      oracle/reference.py:80-82   (np.max, NaN propagates, -inf identity)
  *   softmax  oracle/reference.py:94-106  (exp(x - max) / sum, float64)
+ *   abs-sum  sum of |x| per segment: the scale of the sum tolerance in
+ *            oracle/reference.py:109-174 (np.abs(values) summed per segment)
  * Inputs are f32 or bf16 (raw uint16 bits) values[N, D] and i32/i64
  * offsets[B+1]; outputs are float64, exactly as the reference returns them.
  *
@@ -27,7 +29,7 @@
 #include <omp.h>
 #endif
 
-enum { SO_SUM = 0, SO_MAX = 1, SO_SOFTMAX = 2 };
+enum { SO_SUM = 0, SO_MAX = 1, SO_SOFTMAX = 2, SO_ABSSUM = 3 };
 enum { SO_F32 = 0, SO_BF16 = 1 };
 enum { SO_I32 = 0, SO_I64 = 1 };
 
@@ -70,6 +72,8 @@ static void fold_rows(const void *values, int dtype, int64_t d, int kind, int64_
       for (int64_t j = 0; j < d; ++j) acc[j] += load_value(values, dtype, base + j);
     } else if (kind == SO_MAX) {
       for (int64_t j = 0; j < d; ++j) acc[j] = max_nan(acc[j], load_value(values, dtype, base + j));
+    } else if (kind == SO_ABSSUM) {
+      for (int64_t j = 0; j < d; ++j) acc[j] += fabs(load_value(values, dtype, base + j));
     } else {
       for (int64_t j = 0; j < d; ++j) acc[j] += exp(load_value(values, dtype, base + j) - shift[j]);
     }
@@ -151,10 +155,10 @@ static int reduce_rows(int kind, int dtype, int index_dtype, int64_t n, int64_t 
   return 0;
 }
 
-/* Segmented sum or max: out[B, D] float64.  Returns 0 on success. */
+/* Segmented sum, max or sum of |x|: out[B, D] float64.  Returns 0 on success. */
 int so_segment_reduce(int op, int dtype, int index_dtype, int64_t n, int64_t d, int64_t b,
                       const void *values, const void *offsets, double *out, int threads) {
-  if (op != SO_SUM && op != SO_MAX) return 2;
+  if (op != SO_SUM && op != SO_MAX && op != SO_ABSSUM) return 2;
   return reduce_rows(op, dtype, index_dtype, n, d, b, values, offsets, NULL, out, threads);
 }
 

@@ -77,6 +77,8 @@ int check_device(DeviceProps *props);     // current device must be sm_100
 int launch_naive(const Problem &p, const Geometry &g, cudaStream_t stream, rg_report *report);
 int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
 int launch_rowbal(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
+// Resident CTAs per SM of a row-balanced kernel, cached per (kernel, device).
+int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks);
 int classified_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
 int launch_classified(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
 

@@ -60,11 +60,9 @@ int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 template <typename T, typename OffT, int OP, int VEC>
 int run_typed(const Problem &p, const Geometry &g, const DeviceProps &dev, void *scratch, cudaStream_t stream) {
   int per_sm = 0;
-  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rowbal_kernel<T, OffT, OP, VEC>,
-                                                                    kRowbalThreads, kRowbalSmem),
-                      "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  int status = rowbal_occupancy(reinterpret_cast<const void *>(&rowbal_kernel<T, OffT, OP, VEC>), dev.device,
+                                kRowbalThreads, &per_sm);
   if (status) return status;
-  if (per_sm < 1) per_sm = 1;
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
   const int width = OP == OP_SUM ? 2 : 1;
   const int64_t unit_piece_bytes = 2 * width * p.d * static_cast<int64_t>(sizeof(float));

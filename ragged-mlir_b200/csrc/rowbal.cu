@@ -9,13 +9,13 @@
 namespace rgb {
 
 namespace {
-
 std::mutex g_occupancy_mutex;
 std::map<std::pair<const void *, int>, int> g_occupancy;  // (kernel, device) -> blocks per SM
+}  // namespace
 
-// Opt the kernel into its dynamic shared memory (once per device) and
-// return its resident CTAs per SM.
-int occupancy(const void *kernel, int device, int threads, int *blocks) {
+// Resident CTAs per SM of a row-balanced kernel (kRowbalSmem dynamic shared
+// memory), queried once per (kernel, device) and cached.
+int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks) {
   const auto key = std::make_pair(kernel, device);
   std::lock_guard<std::mutex> lock(g_occupancy_mutex);
   auto it = g_occupancy.find(key);
@@ -31,6 +31,8 @@ int occupancy(const void *kernel, int device, int threads, int *blocks) {
   *blocks = g_occupancy[key];
   return RG_OK;
 }
+
+namespace {
 
 // Resident CTAs per SM requested from ptxas: 3 for sum and max; the softmax
 // statistics (3 floats per feature) get the registers of 2.
@@ -85,7 +87,7 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
   int status = device_props(&dev);
   if (status) return status;
   int per_sm = 0;
-  status = occupancy(kernel, dev.device, kRowbalThreads, &per_sm);
+  status = rowbal_occupancy(kernel, dev.device, kRowbalThreads, &per_sm);
   if (status) return status;
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
   const int64_t path = p.n + p.b;
@@ -99,7 +101,7 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
   plan->packed_ctas = 0;
   if (packed) {
     int packed_per_sm = 0;
-    status = occupancy(packed, dev.device, kRowbalThreads, &packed_per_sm);
+    status = rowbal_occupancy(packed, dev.device, kRowbalThreads, &packed_per_sm);
     if (status) return status;
     const int64_t packed_wanted = (path + 64 * kRowbalThreads - 1) / (64 * kRowbalThreads);
     int64_t ctas = static_cast<int64_t>(packed_per_sm) * dev.sm_count;

@@ -99,6 +99,36 @@ class Workload:
         return values
 
 
+def device_values(w: Workload, rows: tuple[int, int], device) -> "torch.Tensor":  # noqa: F821
+    """Values of rows [lo, hi) of ``w`` generated on a CUDA device with
+    torch's generator, deterministic per chunk of 2^18 rows, so every rank
+    of a sharded call builds exactly its slice of one dataset (the largest
+    configuration does not fit host memory).  bf16 workloads are drawn in
+    bf16 directly; NaN and -inf entries are placed at seeded positions."""
+    import torch
+    lo, hi = rows
+    tdtype = torch.float32 if w.dtype == "f32" else torch.bfloat16
+    out = torch.empty((hi - lo, w.d), dtype=tdtype, device=device)
+    chunk = 1 << 18  # rows per generator chunk
+    for c in range(lo // chunk, (hi + chunk - 1) // chunk):
+        a, b = max(lo, c * chunk), min(hi, (c + 1) * chunk)
+        g = torch.Generator(device=device)
+        g.manual_seed(1_000_003 * w.value_seed + c)
+        block = torch.empty((chunk, w.d), dtype=tdtype, device=device)
+        if w.value_kind == "uniform":
+            block.uniform_(-1.0, 1.0, generator=g)
+        else:
+            block.normal_(0.0, 2.0 if w.value_kind == "normal2" else 1.0, generator=g)
+        if w.nan_fraction or w.neginf_fraction:
+            u = torch.rand(block.shape, generator=g, device=device)
+            block[u < w.nan_fraction] = float("nan")
+            block[(u >= w.nan_fraction) & (u < w.nan_fraction + w.neginf_fraction)] = float("-inf")
+            del u
+        out[a - lo:b - lo] = block[a - c * chunk:b - c * chunk]
+        del block
+    return out
+
+
 def quantize_bf16(values: np.ndarray) -> np.ndarray:
     """f32 -> bf16 RNE (NaN kept), as exact f32 values."""
     values = np.ascontiguousarray(values, dtype=np.float32)

@@ -99,3 +99,27 @@ def check(actual, values, offsets, op, dtype, reference=None):
             reference = rp.REFERENCES[op](values, offsets)
         rp.assert_matches(actual, values, offsets, operation=op, input_dtype=dtype, reference=reference)
         rp.check_strict(actual, values, offsets, operation=op, input_dtype=dtype, reference=reference)
+
+
+def fetcher(tensor):
+    """``fetch(lo, hi)`` for oracle.device_check: rows lo..hi of a torch
+    tensor as the host array the C oracle reads (f32, or bf16 as raw uint16
+    bits), copied a chunk at a time."""
+    import torch
+
+    def fetch(lo, hi):
+        block = tensor[lo:hi]
+        if block.dtype == torch.bfloat16:
+            return block.view(torch.int16).cpu().numpy().view(np.uint16)
+        return block.float().cpu().numpy()
+
+    return fetch
+
+
+def host_rows(out, segments=None) -> np.ndarray:
+    """Output rows (all, or those of ``segments``) as float64 host values."""
+    import torch
+    if segments is None:
+        return out.float().cpu().numpy().astype(np.float64)
+    index = torch.from_numpy(np.asarray(segments, dtype=np.int64)).to(out.device)
+    return out.index_select(0, index).float().cpu().numpy().astype(np.float64)

@@ -1,7 +1,8 @@
 """bench.py's reference arm on the host (no GPU): the JSON line the round
 driver parses, and the rule that only rank 0 of a multi-rank launch runs it.
-The arm times the float64 C oracle (the reference's CPU implementation of
-the path), so it runs here; the GPU arm is covered by the GPU tests.
+The arm times the reference's CPU path (torch.segment_reduce on CPU and the
+float64 C oracle, the faster reported), so it runs here; the GPU arm is
+covered by the GPU tests.
 """
 from __future__ import annotations
 
@@ -47,6 +48,24 @@ def test_reference_line_has_every_contract_key(reference_line):
     assert line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
+    # Both CPU implementations were timed; the line is the one a probe call
+    # found faster, over exactly `steps` calls (the other over 3).
+    legs = line["legs"]
+    assert set(legs) == {"torch", "oracle"}
+    timed = [name for name in legs if legs[name]["calls"] == line["steps"]]
+    assert len(timed) == 1 and legs[timed[0]]["value"] == line["value"]
+
+
+def test_reference_arm_uses_every_host_core_under_torchrun():
+    """torchrun sets OMP_NUM_THREADS=1; the CPU baseline still runs on every
+    core of the process's affinity, at every rank count."""
+    result = run_bench("--impl", "reference", "--workload", "c1", "--scale", "0.01", "--gpus", "4", "--steps", "5",
+                       "--warmup", "1", env={"RANK": "0", "WORLD_SIZE": "4", "LOCAL_RANK": "0",
+                                             "OMP_NUM_THREADS": "1"})
+    assert result.returncode == 0, result.stderr[-2000:]
+    line = json.loads(result.stdout.strip().splitlines()[-1])
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
+    assert line["n_gpus"] == 4 and line["steps"] == 5
 
 
 def test_reference_metric_matches_the_gpu_arm(reference_line):

@@ -181,3 +181,42 @@ def test_masked_logits_rejects_bad_contracts():
         rp.masked_logits(values, np.zeros((1, 2), dtype=np.float32))
     with pytest.raises(ValueError):
         rp.masked_logits(values, None, scale=float("inf"))
+
+
+def test_chunked_checker_matches_whole_oracle():
+    """oracle.device_check (the large-input checker of the GPU tests and of
+    bench.py's parity gate) on host tensors: chunked float64 partials of
+    sum, max and sum |x| equal the whole-array oracle, also for a window of
+    rows; a result one bf16 ulp beyond the bound is rejected."""
+    import torch
+    from helpers import fetcher
+    from oracle import device_check as dc
+    rng = np.random.default_rng(12)
+    lengths = np.array([3, 0, 50, 7, 0, 200, 1, 0, 90, 400], dtype=np.int64)
+    offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    values = rp.quantize_bf16(rng.normal(size=(int(offsets[-1]), 4)).astype(np.float32))
+    values[60, 2] = np.nan
+    host = torch.from_numpy(values).to(torch.bfloat16)
+    fetch = fetcher(host)
+    n = host.shape[0]
+    segments = np.array([0, 1, 2, 3, 5, 6, 8, 9])
+    kinds = ("sum", "max", "abssum")
+    parts = dc.segment_partials(fetch, n, 4, offsets, segments, kinds=kinds, dtype="bf16", chunk_rows=64)
+    for kind, got in zip(kinds, parts):
+        source = np.abs(values) if kind == "abssum" else values
+        with np.errstate(all="ignore"):
+            want = rp.segment_reduce(source, offsets, "max" if kind == "max" else "sum")[segments]
+        np.testing.assert_allclose(got, want, rtol=1e-12, equal_nan=True)
+    window, = dc.segment_partials(fetcher(host[40:300]), 260, 4, offsets, segments, kinds=("sum",), dtype="bf16",
+                                  row_base=40, chunk_rows=30)
+    clipped = values.copy()
+    clipped[:40] = 0
+    clipped[300:] = 0
+    np.testing.assert_allclose(window, rp.segment_sum(clipped, offsets)[segments], rtol=1e-12, equal_nan=True)
+    with np.errstate(all="ignore"):
+        exact = rp.quantize_bf16(rp.segment_sum(values, offsets)[segments].astype(np.float32)).astype(np.float64)
+    dc.check_reduction(exact, fetch, n, offsets, segments, op="sum", dtype="bf16", chunk_rows=64)
+    wrong = exact.copy()
+    wrong[-1, 0] += 4 * rp.bf16_ulp(wrong[-1:, :1])[0, 0]
+    with pytest.raises(AssertionError):
+        dc.check_reduction(wrong, fetch, n, offsets, segments, op="sum", dtype="bf16", chunk_rows=64)
