@@ -4,6 +4,7 @@
 // from the caller's max_len, so a wrong hint cannot under-size it:
 //   state      ClsState counters                       } zeroed by one
 //   done       [splits][col_tiles] u32 chunk counters  } cudaMemsetAsync
+//   late       softmax: [chunks] u32 flags             }
 //   ids        [B] i64 warp-class ids (from the front), CTA-class ids (from the back)
 //   split_seg  [splits] i64,  split_base [splits] i64 (first chunk number)
 //   partials   [chunks][W][D] f32
@@ -11,6 +12,7 @@
 // with T = item_rows (the CTA-class bound and chunk length), splits =
 // min(B, N / (T + 1)) (the reference's B_split rule, docs/classified-abi.md
 // "B_split") and chunks = N / T + splits.
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -27,7 +29,7 @@ int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct ClsLayout {
   int64_t splits, chunks;
-  int64_t state, done, ids, split_seg, split_base, partials, seg_stats, total;
+  int64_t state, done, late, ids, split_seg, split_base, partials, seg_stats, total;
   int64_t memset_bytes;
 };
 
@@ -84,6 +86,8 @@ ClsLayout layout_of(const Problem &p, const Geometry &g) {
   at += align_up(sizeof(ClsState));
   l.done = at;
   at += align_up(l.splits * g.col_tiles * static_cast<int64_t>(sizeof(unsigned)));
+  l.late = at;
+  if (p.op == RG_OP_SOFTMAX) at += align_up(l.chunks * static_cast<int64_t>(sizeof(unsigned)));
   l.memset_bytes = at;
   l.ids = at;
   at += align_up(p.b * 8);
@@ -97,6 +101,19 @@ ClsLayout layout_of(const Problem &p, const Geometry &g) {
   if (p.op == RG_OP_SOFTMAX) at += align_up(l.splits * 2 * p.d * 4);
   l.total = at;
   return l;
+}
+
+// Polls before a worker's wait for a split segment gives up: kChunkWaitPolls,
+// or RAGGED_B200_CHUNK_WAIT_POLLS (read once; 0 makes every wait give up at
+// once, which exercises the late-chunk path of split_normalize_kernel).
+int chunk_wait_polls() {
+  static const int polls = [] {
+    const char *text = std::getenv("RAGGED_B200_CHUNK_WAIT_POLLS");
+    if (!text || !*text) return kChunkWaitPolls;
+    const long value = std::strtol(text, nullptr, 10);
+    return value < 0 ? 0 : (value > kChunkWaitPolls ? kChunkWaitPolls : static_cast<int>(value));
+  }();
+  return polls;
 }
 
 std::mutex g_occ_mutex;
@@ -147,6 +164,31 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
   a.split_base = reinterpret_cast<const int64_t *>(ws + l.split_base);
   a.partials = reinterpret_cast<float *>(ws + l.partials);
   a.seg_stats = reinterpret_cast<float *>(ws + l.seg_stats);
+  a.wait_rows = 0;
+  a.late = reinterpret_cast<unsigned *>(ws + l.late);
+  a.wait_polls = chunk_wait_polls();
+
+  // The pipelined worker's grid (one resident wave).  Softmax split segments
+  // of at most min(kWaitChunks, ctas / 2) chunks are normalised by the
+  // worker itself (classified.cuh, normalized_in_worker: the waiting teams
+  // of the one partly claimed segment then hold stages of fewer than half
+  // the CTAs, so the others keep claiming its chunks).
+  int per_sm = 0;
+  int64_t pipe_ctas = 0;
+  if constexpr (STAGED) {
+    using PL = PipeLayout<OP, VEC>;
+    const void *worker = reinterpret_cast<const void *>(&pipe_worker_kernel<T, OffT, OP, VEC>);
+    status = blocks_per_sm(worker, dev.device, kPipeThreads, PL::kTotalBytes, &per_sm);
+    if (status) return status;
+    pipe_ctas = static_cast<int64_t>(per_sm) * dev.sm_count;
+    const int64_t max_items = (p.b + kPipeClaim - 1) / kPipeClaim + l.chunks;
+    if (pipe_ctas > max_items) pipe_ctas = max_items;
+    if (pipe_ctas < 1) pipe_ctas = 1;
+    if constexpr (OP == OP_SOFTMAX) {
+      const int64_t wait_chunks = pipe_ctas / 2 < kWaitChunks ? pipe_ctas / 2 : kWaitChunks;
+      a.wait_rows = wait_chunks * a.item_rows;
+    }
+  }
 
   status = check_cuda(cudaMemsetAsync(ws, 0, static_cast<size_t>(l.memset_bytes), stream), "cudaMemsetAsync");
   if (status) return status;
@@ -157,24 +199,16 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
   if (cls_blocks > static_cast<int64_t>(dev.sm_count) * 8) cls_blocks = static_cast<int64_t>(dev.sm_count) * 8;
   dim3 cgrid(static_cast<unsigned>(cls_blocks), 1, 1);
   classify_kernel<OffT><<<cgrid, 256, 0, stream>>>(offsets, p.b, a.item_rows, p.op == RG_OP_SOFTMAX, STAGED ? 1 : 0,
-                                                   a.state, reinterpret_cast<int64_t *>(ws + l.ids),
+                                                   a.wait_rows, a.state, reinterpret_cast<int64_t *>(ws + l.ids),
                                                    reinterpret_cast<int64_t *>(ws + l.split_seg),
                                                    reinterpret_cast<int64_t *>(ws + l.split_base));
   record_launch(report, K_CLASSIFY, cgrid, 256, 0);
   status = check_cuda(cudaGetLastError(), "classify_kernel launch");
   if (status) return status;
 
-  int per_sm = 0;
   if constexpr (STAGED) {
     using PL = PipeLayout<OP, VEC>;
-    const void *worker = reinterpret_cast<const void *>(&pipe_worker_kernel<T, OffT, OP, VEC>);
-    status = blocks_per_sm(worker, dev.device, kPipeThreads, PL::kTotalBytes, &per_sm);
-    if (status) return status;
-    int64_t ctas = static_cast<int64_t>(per_sm) * dev.sm_count;
-    const int64_t max_items = (p.b + kPipeClaim - 1) / kPipeClaim + l.chunks;
-    if (ctas > max_items) ctas = max_items;
-    if (ctas < 1) ctas = 1;
-    dim3 wgrid(static_cast<unsigned>(ctas), 1, 1);
+    dim3 wgrid(static_cast<unsigned>(pipe_ctas), 1, 1);
     pipe_worker_kernel<T, OffT, OP, VEC><<<wgrid, kPipeThreads, PL::kTotalBytes, stream>>>(
         static_cast<const T *>(p.values), offsets, static_cast<T *>(p.out), a);
     record_launch(report, K_WORKER, wgrid, kPipeThreads, PL::kTotalBytes);

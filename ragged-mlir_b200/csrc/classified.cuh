@@ -60,6 +60,7 @@ struct ClsState {
   unsigned long long work;         // next work item of the worker
   unsigned long long error;        // nonzero: a bounded wait gave up
   unsigned long long split_work;   // next split chunk of the pipelined worker
+  unsigned long long late_chunks;  // softmax: chunks left to split_normalize_kernel
 };
 
 // Chunk length of a split segment of `len` rows: the item length, or longer
@@ -69,6 +70,35 @@ constexpr int64_t kMaxChunks = 1024;
 __host__ __device__ __forceinline__ int64_t chunk_rows_of(int64_t len, int64_t item_rows) {
   const int64_t spread = (len + kMaxChunks - 1) / kMaxChunks;
   return spread > item_rows ? spread : item_rows;
+}
+
+// Softmax split segments the pipelined worker normalises itself: every
+// chunk is one stage (chunk rows == item rows) and there are at most
+// min(kWaitChunks, worker CTAs / 2) of them.  The team holding a chunk
+// publishes its statistics, waits (bounded) until every chunk of the
+// segment has published, merges them and normalises the chunk's rows
+// straight from its stage, so these rows are read from HBM once.  Longer
+// segments leave their statistics to split_normalize_kernel, which re-reads
+// their rows.
+//
+// Why the wait ends: the worker claims a chunk only after it holds a stage
+// for it, and the team owning that stage reaches it (a team holds one stage
+// at a time), so every claimed chunk publishes its statistics.  Chunks are
+// claimed in list order, so at any moment only one segment can be partly
+// claimed; its waiting teams hold the stages of fewer than half the
+// worker's CTAs, so while those CTAs are resident some producer always
+// reaches the segment's next chunk.  Nothing relies on that residency for
+// correctness: a wait gives up after ClsArgs::wait_polls polls (about a
+// millisecond by default, kChunkWaitPolls; a normal wait lasts a few
+// microseconds; the environment variable RAGGED_B200_CHUNK_WAIT_POLLS
+// overrides the count, so tests can make every wait give up), marks its
+// chunk late and leaves its rows to split_normalize_kernel, which
+// normalises late chunks with the statistics the segment's last chunk
+// writes.
+constexpr int64_t kWaitChunks = 64;
+constexpr int kChunkWaitPolls = 1 << 12;
+__host__ __device__ __forceinline__ bool normalized_in_worker(int64_t len, int64_t item_rows, int64_t wait_rows) {
+  return len <= wait_rows && chunk_rows_of(len, item_rows) == item_rows;
 }
 
 // Floats per feature in a split partial.
@@ -98,17 +128,21 @@ __device__ __forceinline__ int64_t warp_append(bool take, unsigned long long *co
 
 // Segment ids: the warp class fills ids[0, warp_count) upward, the CTA class
 // fills ids[b - cta_count, b) downward, so one [B] array holds both.
+// wait_rows: softmax split segments up to this length are normalised by the
+// worker (normalized_in_worker); the chunks of longer ones are counted in
+// state->late_chunks for split_normalize_kernel.
 template <typename OffT>
 __global__ void __launch_bounds__(256)
 classify_kernel(const OffT *__restrict__ offsets, int64_t b, int64_t item_rows, int softmax, int split_only,
-                ClsState *__restrict__ state, int64_t *__restrict__ ids, int64_t *__restrict__ split_seg,
-                int64_t *__restrict__ split_base) {
+                int64_t wait_rows, ClsState *__restrict__ state, int64_t *__restrict__ ids,
+                int64_t *__restrict__ split_seg, int64_t *__restrict__ split_base) {
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x; base < b; base += stride) {
     const int64_t s = base + threadIdx.x;
     int cls = -1;
     int64_t chunks = 0;
+    bool late = false;
     if (s < b) {
       const int64_t len = static_cast<int64_t>(offsets[s + 1]) - static_cast<int64_t>(offsets[s]);
       if (len <= kWarpClassMax) {
@@ -119,7 +153,14 @@ classify_kernel(const OffT *__restrict__ offsets, int64_t b, int64_t item_rows, 
         cls = 2;
         const int64_t cr = chunk_rows_of(len, item_rows);
         chunks = (len + cr - 1) / cr;
+        late = softmax && !normalized_in_worker(len, item_rows, wait_rows);
       }
+    }
+    if (__any_sync(0xffffffffu, late)) {  // chunks left to the normalise kernel: one atomic per warp
+      int64_t mine = late ? chunks : 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+      if (lane == 0) atomicAdd(&state->late_chunks, static_cast<unsigned long long>(mine));
     }
     if (!split_only) {  // the pipelined worker walks short segments in order and needs no lists
       const int64_t wpos = warp_append(cls == 0, &state->warp_count);
@@ -219,6 +260,9 @@ struct ClsArgs {
   float *partials;     // [chunks][W][D]
   float *seg_stats;    // softmax: [splits][2][D] (reference, total)
   unsigned *done;      // [splits][col_tiles] chunks finished
+  int64_t wait_rows;   // softmax split segments up to this length are normalised by the worker (0: none)
+  unsigned *late;      // softmax: [chunks] nonzero = chunk whose wait gave up (normalised by split_normalize)
+  int wait_polls;      // polls before a wait gives up
 };
 
 // Worker of the classified schedule for rows that cannot be staged by bulk
@@ -378,6 +422,7 @@ split_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ of
   const int G = 1 << a.g_shift;
   const int q = lane >> a.g_shift, cl = lane & (G - 1);
   const int upw = 32 >> a.g_shift;
+  if (__ldcg(&a.state->late_chunks) == 0) return;  // the worker normalised every split segment
   const unsigned long long packed = __ldcg(&a.state->split_packed);
   const int64_t n_split = static_cast<int64_t>(packed & kSplitCountMask);
   const int64_t n_chunks = static_cast<int64_t>(packed >> kSplitCountBits);
@@ -402,6 +447,8 @@ split_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ of
     const int64_t index = lo;
     const int64_t seg = __ldcg(a.split_seg + index), first = __ldcg(a.split_base + index);
     const int64_t begin = static_cast<int64_t>(offsets[seg]), end = static_cast<int64_t>(offsets[seg + 1]);
+    if (normalized_in_worker(end - begin, a.item_rows, a.wait_rows) && __ldcg(a.late + c) == 0)
+      continue;  // normalised by the worker (uniform per warp)
     const int64_t cr = chunk_rows_of(end - begin, a.item_rows);
     const int64_t r0 = begin + (c - first) * cr;
     const int64_t r1 = r0 + cr < end ? r0 + cr : end;

@@ -375,6 +375,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return done != 0;
 }
 
+// Acquire load of a counter other CTAs increment (a spin-wait's poll).
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Bounded wait for phase `parity` of `bar` (each try_wait itself suspends
 // for a while); false after the limit, so a lost transaction cannot hang
 // the GPU.

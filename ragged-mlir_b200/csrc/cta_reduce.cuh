@@ -39,13 +39,15 @@ struct GlobalRows {
 template <typename T, int VEC>
 struct SharedRows {
   using Raw = typename VecIO<T, VEC>::Raw;
-  const char *base;
+  char *base;
   int64_t row0;
   int row_bytes, col_bytes;
   struct Cursor {
-    const char *p;
+    char *p;
     int stride;
     __device__ __forceinline__ Raw raw(int k) const { return *reinterpret_cast<const Raw *>(p + k * stride); }
+    // Overwrite the k-th vector (the softmax mass pass keeps its terms there).
+    __device__ __forceinline__ void put(int k, const Raw &v) const { *reinterpret_cast<Raw *>(p + k * stride) = v; }
   };
   __device__ __forceinline__ Cursor at(int64_t r, int64_t step) const {
     return Cursor{base + static_cast<int>(r - row0) * row_bytes + col_bytes, static_cast<int>(step) * row_bytes};
@@ -189,6 +191,126 @@ __device__ __forceinline__ void staged_stats(Acc<OP_SOFTMAX, VEC> &acc, const Sr
   }
 #pragma unroll
   for (int v = 0; v < VEC; ++v) acc.st[v] = Stats{m[v], s[v], 0.0f};
+}
+
+// VEC f32 values in the raw form of T (bf16: round to nearest even).
+template <typename T, int VEC>
+__device__ __forceinline__ typename VecIO<T, VEC>::Raw pack_raw(const float (&y)[VEC]) {
+  using Raw = typename VecIO<T, VEC>::Raw;
+  Raw raw;
+  if constexpr (std::is_same<T, float>::value) {
+    static_assert(sizeof(Raw) == VEC * 4, "f32 raw form");
+    memcpy(&raw, y, sizeof raw);
+  } else if constexpr (VEC == 8) {
+    raw = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                     pack_bf16x2(y[6], y[7]));
+  } else if constexpr (VEC == 4) {
+    raw = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+  } else if constexpr (VEC == 2) {
+    raw = pack_bf16x2(y[0], y[1]);
+  } else {
+    const __nv_bfloat16 h = __float2bfloat16_rn(y[0]);
+    raw = *reinterpret_cast<const unsigned short *>(&h);
+  }
+  return raw;
+}
+
+// Softmax statistics of a thread's staged rows, like staged_stats, that
+// also keep every term e = e^(x - b) in the stage in place of x (in T: a
+// bf16 term is rounded once more), so the normalisation multiplies instead
+// of recomputing the exponential: out = e * e^(b - M) / total, with b the
+// thread's own maximum (0 when every value it saw is -inf) returned in
+// `base`.  Keeping the terms halves the SFU work of a staged softmax; for
+// bf16 output the extra rounding keeps the result within one ulp of the
+// rounded exact value (a half-ulp error on e, then the final rounding).
+template <typename T, int VEC>
+__device__ __forceinline__ void staged_stats_keep(Acc<OP_SOFTMAX, VEC> &acc, const SharedRows<T, VEC> &src,
+                                                  int64_t begin, int64_t end, int64_t row_lane, int64_t step,
+                                                  float (&base)[VEC]) {
+  constexpr int U = kFoldUnroll;
+  using Raw = typename VecIO<T, VEC>::Raw;
+  static_assert(VEC % 2 == 0, "packed pairs");
+  constexpr int P = VEC / 2;
+  float m[VEC], s[VEC];
+  rows_max<T, VEC>(m, src, begin, end, row_lane, step);
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) base[v] = m[v] == -kInf ? 0.0f : m[v];  // all -inf: every term is e^-inf = 0
+  unsigned long long b2[P], s2[P];
+#pragma unroll
+  for (int k = 0; k < P; ++k) {
+    b2[k] = pack2(base[2 * k], base[2 * k + 1]);
+    s2[k] = pack2(0.0f, 0.0f);
+  }
+  const int count = lane_rows(begin, end, row_lane, step);
+  const auto cur = src.at(begin + row_lane, step);
+  auto keep_row = [&](const Raw &raw, int k) {
+    float x[VEC], e[VEC];
+    VecIO<T, VEC>::unpack(raw, x);
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const unsigned long long t = exp_diff2(pack2(x[2 * j], x[2 * j + 1]), b2[j]);
+      s2[j] = add2_rn(s2[j], t);
+      unpack2(t, e[2 * j], e[2 * j + 1]);
+    }
+    cur.put(k, pack_raw<T, VEC>(e));
+  };
+  int k = 0;
+  for (; k + U <= count; k += U) {
+    Raw raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) raw[u] = cur.raw(k + u);
+#pragma unroll
+    for (int u = 0; u < U; ++u) keep_row(raw[u], k + u);
+  }
+  for (; k < count; ++k) keep_row(cur.raw(k), k);
+#pragma unroll
+  for (int j = 0; j < P; ++j) unpack2(s2[j], s[2 * j], s[2 * j + 1]);
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) acc.st[v] = Stats{m[v], s[v], 0.0f};
+}
+
+// Factor of the kept terms of a thread: e^(base - ref) / total per
+// feature.  A thread whose values were all -inf kept zeros: its factor is
+// 0 * inv, which stays NaN for a column that is -inf throughout (total 0).
+template <int VEC>
+__device__ __forceinline__ void kept_factor(const float (&base)[VEC], const float (&m)[VEC], const float (&ref)[VEC],
+                                            const float (&inv)[VEC], float (&f)[VEC]) {
+#pragma unroll
+  for (int v = 0; v < VEC; ++v)
+    f[v] = m[v] == -kInf ? __fmul_rn(0.0f, inv[v]) : __fmul_rn(exp_diff(base[v], ref[v]), inv[v]);
+}
+
+// Normalise kept rows [begin, end): out = term * f per feature.
+template <typename T, int VEC>
+__device__ __forceinline__ void normalize_kept(const SharedRows<T, VEC> &src, T *__restrict__ out, int64_t d,
+                                               int64_t col, int64_t begin, int64_t end, int64_t row_lane,
+                                               int64_t step, const float (&f)[VEC]) {
+  constexpr int U = kFoldUnroll;
+  using Raw = typename VecIO<T, VEC>::Raw;
+  constexpr int P = VEC / 2;
+  unsigned long long f2[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) f2[j] = pack2(f[2 * j], f[2 * j + 1]);
+  const int count = lane_rows(begin, end, row_lane, step);
+  const auto cur = src.at(begin + row_lane, step);
+  T *const o = out + (begin + row_lane) * d + col;
+  const int64_t ostride = step * d;
+  auto scale_row = [&](const Raw &raw, int k) {
+    float x[VEC], y[VEC];
+    VecIO<T, VEC>::unpack(raw, x);
+#pragma unroll
+    for (int j = 0; j < P; ++j) unpack2(mul2_rn(pack2(x[2 * j], x[2 * j + 1]), f2[j]), y[2 * j], y[2 * j + 1]);
+    VecIO<T, VEC>::store(o + k * ostride, y);
+  };
+  int k = 0;
+  for (; k + U <= count; k += U) {
+    Raw raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) raw[u] = cur.raw(k + u);
+#pragma unroll
+    for (int u = 0; u < U; ++u) scale_row(raw[u], k + u);
+  }
+  for (; k < count; ++k) scale_row(cur.raw(k), k);
 }
 
 // Merge the row groups of each warp, then the NW warps, leaving the result

@@ -61,7 +61,10 @@ constexpr int kPipeTeams = kPipeConsumerWarps / kPipeTeamWarps;
 constexpr int kPipeThreads = 32 * (kPipeConsumerWarps + 1);
 constexpr int kPipeProducer = kPipeConsumerWarps;  // warp index of the producer
 constexpr int kPipeClaim = 32;                     // segments claimed per atomic
-constexpr int kSmemBudget = 227 * 1024;
+#ifndef RG_PIPE_SMEM_KB
+#define RG_PIPE_SMEM_KB 227
+#endif
+constexpr int kSmemBudget = RG_PIPE_SMEM_KB * 1024;
 constexpr uint32_t kPieceBytes = 4096;  // bytes per bulk-copy request (a multiple of 16)
 
 // The same stage count for every op.
@@ -82,18 +85,26 @@ struct StageRecord {
   int64_t index, first, chunks;  // SPLIT: split-list index, first chunk number, chunk count
   int64_t chunk;       // SPLIT: chunk number
   int32_t chunk_first, chunk_last;  // SPLIT: this stage starts / ends its chunk
+  int32_t wait;        // SPLIT (softmax): the team waits for the segment and normalises the stage
+  int32_t pad2;
   int64_t ends[kPipeClaim];      // RUN: end row of each segment of the run
 };
 
+// Shared memory: the stages, their records, the barriers and, for softmax,
+// one merge area per team (a team that normalises a split chunk from its
+// stage merges its warps' statistics there, leaving the rows intact; the
+// other ops merge inside the stage they hold).
 template <int OP, int VEC>
 struct PipeLayout {
   static constexpr int kStages = PipeStages<OP>::value;
   static constexpr int kRecordBytes = kStages * static_cast<int>(sizeof(StageRecord));
   static constexpr int kBarrierBytes = 2 * kStages * 8 + 64;
-  static constexpr int kStageBytes = ((kSmemBudget - kRecordBytes - kBarrierBytes - 256) / kStages) / 1024 * 1024;
-  static constexpr int kTotalBytes = kStages * kStageBytes + kRecordBytes + kBarrierBytes + 128;
-  // A team merges its warps' partials in the stage it holds (team_merge).
-  static_assert(kStageBytes >= kPipeTeamWarps * 32 * static_cast<int>(sizeof(Acc<OP, VEC>)), "stage too small");
+  static constexpr int kTeamScratch = kPipeTeamWarps * 32 * static_cast<int>(sizeof(Acc<OP, VEC>));
+  static constexpr int kScratchBytes = OP == OP_SOFTMAX ? kPipeTeams * kTeamScratch : 0;
+  static constexpr int kStageBytes =
+      ((kSmemBudget - kRecordBytes - kBarrierBytes - kScratchBytes - 256) / kStages) / 1024 * 1024;
+  static constexpr int kTotalBytes = kStages * kStageBytes + kRecordBytes + kBarrierBytes + kScratchBytes + 128;
+  static_assert(kStageBytes >= kTeamScratch, "stage too small");
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -138,7 +149,10 @@ __device__ __forceinline__ void fold_staged(Acc<OP, VEC> &acc, const Src &src, i
 }
 
 template <typename T, typename OffT, int OP, int VEC>
-__global__ void __launch_bounds__(kPipeThreads, 1)
+#ifndef RG_PIPE_MIN_BLOCKS
+#define RG_PIPE_MIN_BLOCKS 1
+#endif
+__global__ void __launch_bounds__(kPipeThreads, RG_PIPE_MIN_BLOCKS)
 pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out, ClsArgs a) {
   using L = PipeLayout<OP, VEC>;
   constexpr int S = L::kStages;
@@ -150,6 +164,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
   uint64_t *const full = reinterpret_cast<uint64_t *>(smem + S * L::kStageBytes + L::kRecordBytes);
   uint64_t *const empty = full + S;
   int *const last_flag = reinterpret_cast<int *>(empty + S);  // [kPipeTeams]
+  char *const scratch = smem + S * L::kStageBytes + L::kRecordBytes + L::kBarrierBytes;  // softmax team merges
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t d = a.d;
@@ -254,11 +269,12 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       o0 = n0;
       o1 = n1;
     }
-    // Split chunks in chunk order, kSplitClaim per atomic (the next claim in
-    // flight); each chunk is published as consecutive stages for one team.
-    // Lane l caches split entry wbase + l (first chunk, segment, rows), so
-    // walking consecutive chunks needs no search.
-    constexpr int kSplitClaim = 4;
+    // Split chunks in chunk order, one per atomic, claimed only once the
+    // stage for it is held (a claimed chunk always reaches its team: the
+    // waits of normalized_in_worker rely on it).  Each chunk is published as
+    // consecutive stages for one team.  Lane l caches split entry wbase + l
+    // (first chunk, segment, rows), so walking consecutive chunks needs no
+    // search.
     int64_t wbase = -1, w_first = INT64_MAX, w_seg = 0, w_begin = 0, w_end = 0, w_rows = 1, w_chunks = 0;
     auto load_window = [&](int64_t start) {
       wbase = start;
@@ -276,63 +292,60 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       const unsigned m = __ballot_sync(0xffffffffu, w_first <= c && c < w_first + w_chunks);
       return m ? __ffs(m) - 1 : -1;
     };
-    if (lane == 0) pending = atomicAdd(&a.state->split_work, static_cast<unsigned long long>(kSplitClaim));
-    for (;;) {
-      const int64_t c0 = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
-      if (c0 >= n_chunks) break;
-      if (lane == 0) pending = atomicAdd(&a.state->split_work, static_cast<unsigned long long>(kSplitClaim));
-      const int64_t c1 = c0 + kSplitClaim < n_chunks ? c0 + kSplitClaim : n_chunks;
-      for (int64_t c = c0; c < c1; ++c) {
-        int k = find(c);
-        if (k < 0) {
-          // 32-ary search of the split list for the last i with base[i] <= c.
-          int64_t lo = 0, hi = n_split - 1;
-          while (lo < hi) {
-            const int64_t step = (hi - lo + 31) / 32;
-            const int64_t probe = lo + (lane + 1) * step;
-            const bool le = probe <= hi && __ldcg(a.split_base + probe) <= c;
-            const unsigned m = __ballot_sync(0xffffffffu, le);
-            const int n = m ? 32 - __clz(m) : 0;  // probes lo + 1..n*step are <= c
-            const int64_t cut = lo + static_cast<int64_t>(n + 1) * step - 1;
-            hi = n < 32 && cut < hi ? cut : hi;
-            lo = lo + static_cast<int64_t>(n) * step;
-          }
-          load_window(lo);
-          k = find(c);
-        }
-        const int64_t seg = __shfl_sync(0xffffffffu, w_seg, k);
-        const int64_t first = __shfl_sync(0xffffffffu, w_first, k);
-        const int64_t begin = __shfl_sync(0xffffffffu, w_begin, k);
-        const int64_t end = __shfl_sync(0xffffffffu, w_end, k);
-        const int64_t rows_per_chunk = __shfl_sync(0xffffffffu, w_rows, k);
-        const int64_t chunks = __shfl_sync(0xffffffffu, w_chunks, k);
-        const int64_t r0 = begin + (c - first) * rows_per_chunk;
-        const int64_t r1 = r0 + rows_per_chunk < end ? r0 + rows_per_chunk : end;
-        for (int64_t a0 = r0; a0 < r1; a0 += a.item_rows) {
-          const int64_t a1 = a0 + a.item_rows < r1 ? a0 + a.item_rows : r1;
-          int s;
-          acquire(s);
-          if (lane == 0) {
-            StageRecord &r = rec[s];
-            r.kind = STAGE_SPLIT;
-            r.team = team;
-            r.seg = seg;
-            r.r0 = a0;
-            r.r1 = a1;
-            r.index = wbase + k;
-            r.first = first;
-            r.chunks = chunks;
-            r.chunk = c;
-            r.chunk_first = a0 == r0;
-            r.chunk_last = a1 == r1;
-          }
-          publish(s, values + a0 * d, static_cast<uint32_t>((a1 - a0) * a.row_bytes));
-        }
-        team = team + 1 == kPipeTeams ? 0 : team + 1;
-      }
-    }
     int s;
-    acquire(s);
+    for (;;) {
+      acquire(s);
+      if (lane == 0) pending = atomicAdd(&a.state->split_work, 1ull);
+      const int64_t c = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
+      if (c >= n_chunks) break;  // stage s stays acquired for the DONE record
+      int k = find(c);
+      if (k < 0) {
+        // 32-ary search of the split list for the last i with base[i] <= c.
+        int64_t lo = 0, hi = n_split - 1;
+        while (lo < hi) {
+          const int64_t step = (hi - lo + 31) / 32;
+          const int64_t probe = lo + (lane + 1) * step;
+          const bool le = probe <= hi && __ldcg(a.split_base + probe) <= c;
+          const unsigned m = __ballot_sync(0xffffffffu, le);
+          const int n = m ? 32 - __clz(m) : 0;  // probes lo + 1..n*step are <= c
+          const int64_t cut = lo + static_cast<int64_t>(n + 1) * step - 1;
+          hi = n < 32 && cut < hi ? cut : hi;
+          lo = lo + static_cast<int64_t>(n) * step;
+        }
+        load_window(lo);
+        k = find(c);
+      }
+      const int64_t seg = __shfl_sync(0xffffffffu, w_seg, k);
+      const int64_t first = __shfl_sync(0xffffffffu, w_first, k);
+      const int64_t begin = __shfl_sync(0xffffffffu, w_begin, k);
+      const int64_t end = __shfl_sync(0xffffffffu, w_end, k);
+      const int64_t rows_per_chunk = __shfl_sync(0xffffffffu, w_rows, k);
+      const int64_t chunks = __shfl_sync(0xffffffffu, w_chunks, k);
+      const int64_t r0 = begin + (c - first) * rows_per_chunk;
+      const int64_t r1 = r0 + rows_per_chunk < end ? r0 + rows_per_chunk : end;
+      const bool wait = OP == OP_SOFTMAX && normalized_in_worker(end - begin, a.item_rows, a.wait_rows);
+      for (int64_t a0 = r0; a0 < r1; a0 += a.item_rows) {
+        const int64_t a1 = a0 + a.item_rows < r1 ? a0 + a.item_rows : r1;
+        if (a0 != r0) acquire(s);  // later stages of a chunk longer than one stage
+        if (lane == 0) {
+          StageRecord &r = rec[s];
+          r.kind = STAGE_SPLIT;
+          r.team = team;
+          r.seg = seg;
+          r.r0 = a0;
+          r.r1 = a1;
+          r.index = wbase + k;
+          r.first = first;
+          r.chunks = chunks;
+          r.chunk = c;
+          r.chunk_first = a0 == r0;
+          r.chunk_last = a1 == r1;
+          r.wait = wait;
+        }
+        publish(s, values + a0 * d, static_cast<uint32_t>((a1 - a0) * a.row_bytes));
+      }
+      team = team + 1 == kPipeTeams ? 0 : team + 1;
+    }
     if (lane == 0) rec[s].kind = STAGE_DONE;
     publish(s, nullptr, 0);
     if (!ok && lane == 0) atomicExch(&a.state->error, 1ull);
@@ -374,18 +387,28 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         if ((owner < kPipeTeamWarps ? owner : kPipeTeamWarps - 1) == wit) {
           Acc<OP, VEC> acc;
           acc.init();
-          if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, q, warp_step);
-          warp_merge<OP, VEC>(acc, G);
           if constexpr (OP == OP_SOFTMAX) {
+            // The mass pass keeps its terms in the stage; the normalisation
+            // scales them by e^(base - M) / total.
+            float base[VEC], mine[VEC];
+            if (active) staged_stats_keep<T, VEC>(acc, rows, begin, end, q, warp_step, base);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) mine[v] = acc.st[v].r;
+            warp_merge<OP, VEC>(acc, G);
             if (active) {
-              float ref[VEC], inv[VEC];
+              float ref[VEC], inv[VEC], f[VEC];
               stats_of<VEC>(acc, ref, inv);
-              normalize_rows<T, VEC>(rows, out, d, col, begin, end, q, warp_step, ref, inv);
+              kept_factor<VEC>(base, mine, ref, inv, f);
+              normalize_kept<T, VEC>(rows, out, d, col, begin, end, q, warp_step, f);
             }
-          } else if (q == 0 && active) {
-            float y[VEC];
-            acc.result(y);
-            VecIO<T, VEC>::store(out + seg * d + col, y);
+          } else {
+            if (active) fold_staged<T, OP, VEC>(acc, rows, begin, end, q, warp_step);
+            warp_merge<OP, VEC>(acc, G);
+            if (q == 0 && active) {
+              float y[VEC];
+              acc.result(y);
+              VecIO<T, VEC>::store(out + seg * d + col, y);
+            }
           }
         }
         begin = end;
@@ -395,10 +418,13 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       // f32 partial, and the team finishing the segment's last chunk merges
       const int64_t c = r.chunk, index = r.index, first = r.first, chunks = r.chunks, seg = r.seg;
       if (r.chunk_first) split_acc.init();
+      float base[VEC], mine[VEC];  // softmax: the thread's kept terms are e^(x - base); mine = its maximum
       if (active) {
         if constexpr (OP == OP_SOFTMAX) {
           Acc<OP, VEC> stage_acc;
-          staged_stats<T, VEC>(stage_acc, rows, r.r0, r.r1, team_lane, team_step);
+          staged_stats_keep<T, VEC>(stage_acc, rows, r.r0, r.r1, team_lane, team_step, base);
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) mine[v] = stage_acc.st[v].r;
           split_acc.merge(stage_acc);
         } else {
           fold_rows<T, OP, VEC>(split_acc, rows, r.r0, r.r1, team_lane, team_step);
@@ -409,49 +435,66 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         if (lane == 0) mbar_arrive(&empty[s]);
         continue;
       }
-      Acc<OP, VEC> *const part = reinterpret_cast<Acc<OP, VEC> *>(stages + static_cast<int64_t>(s) * L::kStageBytes);
+      // Softmax merges in the team's own area, so a waiting chunk's rows stay
+      // in its stage; the other ops merge inside the stage they hold.
+      Acc<OP, VEC> *const part = reinterpret_cast<Acc<OP, VEC> *>(
+          OP == OP_SOFTMAX ? scratch + team * L::kTeamScratch : stages + static_cast<int64_t>(s) * L::kStageBytes);
       Acc<OP, VEC> acc = split_acc;
       team_merge<OP, VEC>(acc, part, team, wit, q, cl, G);
       if (wit == 0 && q == 0 && active) store_partial<OP, VEC>(acc, a.partials + (c * W) * d + col, d);
       __threadfence();  // release: the partial before the count
       named_sync(1 + team, 32 * kPipeTeamWarps);
-      if (wit == 0 && lane == 0) last_flag[team] = atomicAdd(a.done + index, 1u) == static_cast<unsigned>(chunks - 1);
+      bool wait = OP == OP_SOFTMAX && r.wait;
+      if (wit == 0 && lane == 0) {
+        const bool last = atomicAdd(a.done + index, 1u) == static_cast<unsigned>(chunks - 1);
+        int flag = last ? 1 : 0;
+        if (wait && !last) {  // bounded wait until every chunk of the segment has published
+          bool complete = ld_acquire_gpu(a.done + index) >= static_cast<unsigned>(chunks);
+          for (int i = 0; !complete && i < a.wait_polls; ++i) {
+            __nanosleep(256);
+            complete = ld_acquire_gpu(a.done + index) >= static_cast<unsigned>(chunks);
+          }
+          if (!complete) {  // gave up: split_normalize_kernel normalises this chunk
+            a.late[c] = 1u;
+            atomicAdd(&a.state->late_chunks, 1ull);
+            flag |= 2;
+          }
+        }
+        last_flag[team] = flag;
+      }
       named_sync(1 + team, 32 * kPipeTeamWarps);
-      if (last_flag[team]) {
+      const int flag = last_flag[team];
+      if (flag & 2) wait = false;
+      if ((flag & 1) || wait) {
         __threadfence();  // acquire: every chunk's partial is visible
         Acc<OP, VEC> m;
         m.init();
-        if (active) {
-          int64_t j = first + team_lane;
-          for (; j + 3 * team_step < first + chunks; j += 4 * team_step) {
-            Acc<OP, VEC> p0, p1, p2, p3;  // four loads in flight
-            load_partial<OP, VEC>(p0, a.partials + (j * W) * d + col, d);
-            load_partial<OP, VEC>(p1, a.partials + ((j + team_step) * W) * d + col, d);
-            load_partial<OP, VEC>(p2, a.partials + ((j + 2 * team_step) * W) * d + col, d);
-            load_partial<OP, VEC>(p3, a.partials + ((j + 3 * team_step) * W) * d + col, d);
-            p0.merge(p1);
-            p2.merge(p3);
-            p0.merge(p2);
-            m.merge(p0);
-          }
-          for (; j < first + chunks; j += team_step) {
+        if (active) {  // one partial at a time: a merge runs once per segment, registers matter more
+          for (int64_t j = first + team_lane; j < first + chunks; j += team_step) {
             Acc<OP, VEC> pj;
             load_partial<OP, VEC>(pj, a.partials + (j * W) * d + col, d);
             m.merge(pj);
           }
         }
         team_merge<OP, VEC>(m, part, team, wit, q, cl, G);
-        if (wit == 0 && q == 0 && active) {
-          if constexpr (OP == OP_SOFTMAX) {
+        if constexpr (OP == OP_SOFTMAX) {
+          // The last chunk also leaves the statistics for the normalise kernel
+          // (every chunk of a long segment, a chunk whose wait gave up).
+          if ((flag & 1) && wit == 0 && q == 0 && active)
             store_partial<OP, VEC>(m, a.seg_stats + index * 2 * d + col, d);
-          } else {
-            float y[VEC];
-            m.result(y);
-            VecIO<T, VEC>::store(out + seg * d + col, y);
+          if (wait && active) {  // every team of the segment merged the same partials in the same order
+            float ref[VEC], inv[VEC], f[VEC];
+            stats_of<VEC>(m, ref, inv);
+            kept_factor<VEC>(base, mine, ref, inv, f);
+            normalize_kept<T, VEC>(rows, out, d, col, r.r0, r.r1, team_lane, team_step, f);
           }
+        } else if (wit == 0 && q == 0 && active) {
+          float y[VEC];
+          m.result(y);
+          VecIO<T, VEC>::store(out + seg * d + col, y);
         }
       }
-      fence_proxy_async_shared();  // the partials written into the stage, before its next bulk copy
+      if constexpr (OP != OP_SOFTMAX) fence_proxy_async_shared();  // partials written into the stage
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
