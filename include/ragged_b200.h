@@ -83,6 +83,11 @@ typedef struct rg_report {
   int32_t streams;                        /* streams used (1: caller's only)  */
   int64_t workspace_bytes;                /* scratch the call required        */
   int64_t thresholds[2];                  /* classified: warp- and CTA-class length bounds (rows) */
+  /* Byte offset in the workspace of the call's device status word (int64;
+   * nonzero once the stream has run the call means a bounded wait inside
+   * a kernel gave up and the call's results are undefined), or -1 when the
+   * schedule keeps none.  Checked mode reads it back after the call. */
+  int64_t status_offset;
 } rg_report;
 
 typedef struct rg_device_info {

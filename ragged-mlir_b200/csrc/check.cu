@@ -63,6 +63,7 @@ extern "C" int rg_check_offsets(int index_dtype, int64_t n, int64_t b, const voi
                                 int64_t max_len, int64_t *status, void *stream, rg_report *report) {
   if (report) {
     std::memset(report, 0, sizeof *report);
+    report->status_offset = -1;
     report->streams = 1;
   }
   if (index_dtype != RG_INDEX_I32 && index_dtype != RG_INDEX_I64)

@@ -12,6 +12,7 @@
 // with T = item_rows (the CTA-class bound and chunk length), splits =
 // min(B, N / (T + 1)) (the reference's B_split rule, docs/classified-abi.md
 // "B_split") and chunks = N / T + splits.
+#include <cstddef>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -298,6 +299,7 @@ int launch_classified(const Problem &p, const Geometry &g, void *workspace, cuda
   if (report) {
     report->thresholds[0] = kWarpClassMax;
     report->thresholds[1] = item_rows_of(p, g);
+    report->status_offset = static_cast<int64_t>(offsetof(ClsState, error));  // ClsState sits at offset 0
   }
   char *ws = static_cast<char *>(workspace);
   return p.dtype == RG_DTYPE_F32 ? launch_index<float>(p, g, ws, stream, report)

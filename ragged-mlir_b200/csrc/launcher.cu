@@ -257,6 +257,7 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b, 
   Problem p{op, dtype, index_dtype, d, n, b, values, offsets, out, max_len, flags};
   if (report) {
     std::memset(report, 0, sizeof *report);
+    report->status_offset = -1;
     report->schedule = schedule;
     report->streams = 1;
   }

@@ -205,6 +205,7 @@ int rg_run_pointwise(int op, int dtype, int index_dtype, int64_t d, int64_t n, i
   Problem p{op, dtype, index_dtype, d, n, b, values, offsets, out, max_len, flags};
   if (report) {
     std::memset(report, 0, sizeof *report);
+    report->status_offset = -1;
     report->schedule = schedule;
     report->streams = 1;
   }
@@ -248,6 +249,7 @@ int rg_run_pointwise(int op, int dtype, int index_dtype, int64_t d, int64_t n, i
     report->d_tile = 1 << g.g_shift;
   }
   status = run_schedule(q, g, schedule, ws + l.inner_offset, s, report);
+  if (report && report->status_offset >= 0) report->status_offset += l.inner_offset;
   if (status || dtype == RG_DTYPE_F32) return status;
   const int64_t rows_out = op == RG_OP_SOFTMAX ? n : b;
   return launch_cast(results, out, rows_out * d, dev, s, report);

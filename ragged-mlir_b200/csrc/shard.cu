@@ -362,6 +362,7 @@ int rg_run_shard(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64
                  void *workspace, int64_t workspace_bytes, uint32_t flags, void *stream, rg_report *report) {
   if (report) {
     std::memset(report, 0, sizeof *report);
+    report->status_offset = -1;
     report->schedule = RG_SCHEDULE_ROWBALANCED;
     report->streams = 1;
   }
@@ -521,6 +522,7 @@ int rg_run_shard_softmax(int dtype, int index_dtype, int64_t d, int64_t n, int64
                          rg_report *report) {
   if (report) {
     std::memset(report, 0, sizeof *report);
+    report->status_offset = -1;
     report->schedule = RG_SCHEDULE_ROWBALANCED;
     report->streams = 1;
   }
@@ -549,6 +551,7 @@ int rg_shard_softmax_finish(int dtype, int index_dtype, int64_t d, int64_t n, in
                             void *stream, rg_report *report) {
   if (report) {
     std::memset(report, 0, sizeof *report);
+    report->status_offset = -1;
     report->schedule = RG_SCHEDULE_ROWBALANCED;
     report->streams = 1;
   }

@@ -42,7 +42,7 @@ class Report(ctypes.Structure):
                 ("block", ctypes.c_int32 * MAX_LAUNCHES), ("shared_bytes", ctypes.c_int32 * MAX_LAUNCHES),
                 ("memsets", ctypes.c_int32), ("d_vector", ctypes.c_int32), ("d_tile", ctypes.c_int32),
                 ("streams", ctypes.c_int32), ("workspace_bytes", ctypes.c_int64),
-                ("thresholds", ctypes.c_int64 * 2)]
+                ("thresholds", ctypes.c_int64 * 2), ("status_offset", ctypes.c_int64)]
 
 
 class DeviceInfo(ctypes.Structure):

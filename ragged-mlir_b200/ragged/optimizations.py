@@ -45,6 +45,18 @@ class Optimizations:
     def to_dict(self):
         return asdict(self)
 
+    def effects(self, *, transformed: bool = False) -> dict[str, list[str]]:
+        """Which requested controls change what a call runs ("applied") and
+        which are accepted but change nothing on B200 ("no_effect"); every
+        ExecutionReport carries this next to the request.  ``transformed``:
+        the call has a scale or mask, the only case pointwise_fusion
+        selects anything for."""
+        applied = ["classification", "vectorize"]
+        if transformed:
+            applied.append("pointwise_fusion")
+        ignored = [name for name in BOOL_OPTIONS if name not in applied] + ["feature_tile"]
+        return {"applied": applied, "no_effect": ignored}
+
     def geometry(self, d: int, dtype: str = "f32") -> tuple[int, int]:
         """(d_tile, d_vector) of the B200 kernels: each thread owns d_vector
         adjacent features (the largest power of two dividing D that fits 16

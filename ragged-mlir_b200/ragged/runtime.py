@@ -267,7 +267,24 @@ class CompiledProgram:
                 report = _native.run(self.spec.op, self.spec.dtype, self.spec.offsets_dtype, self.spec.feature_dim,
                                      n, b, values.data_ptr(), offsets.data_ptr(), out.data_ptr(), base, nbytes,
                                      schedule, max_len, self._flags, active.cuda_stream)
+            if checked and scratch is not None and getattr(report, "status_offset", -1) >= 0:
+                self._check_device_status(scratch, int(report.status_offset), active, torch)
         return self._report(schedule, selection, started, report, nbytes, validation)
+
+    @staticmethod
+    def _check_device_status(scratch, offset, active, torch):
+        """Checked mode, after the launch: read the call's device status word
+        (rg_report.status_offset into the scratch) and raise when a bounded
+        wait inside a kernel gave up, since the results are then undefined.
+        Validated mode never reads it (no synchronisation)."""
+        with torch.cuda.stream(active):
+            host = torch.empty((1,), dtype=torch.int64, device="cpu", pin_memory=True)
+            host.copy_(scratch.narrow(0, offset, 8).view(torch.int64), non_blocking=True)
+        active.synchronize()
+        word = int(host.tolist()[0])
+        if word:
+            raise RuntimeError(f"a bounded wait inside the kernel gave up (device status {word}); the call's results "
+                               "are undefined")
 
     def _check_offsets(self, values, offsets, n, b, active, torch):
         """Checked mode (reference python/ragged/runtime.py:506-533): validate
@@ -431,6 +448,7 @@ class CompiledProgram:
                                (time.perf_counter() - started) * 1000, cache_hit=self.cache_hit,
                                validation_workspace_bytes=checked_bytes,
                                validation_host_ms=validation_ms if validation is not None else None,
-                               optimizations={"requested": self.spec.optimizations.to_dict()},
+                               optimizations={"requested": self.spec.optimizations.to_dict(),
+                                              **self.spec.optimizations.effects(transformed=self._pointwise)},
                                pointwise_materialized=self._pointwise,
                                d_tile=tile, d_vector=vec, streams=streams, selected=schedule, selection=selection)

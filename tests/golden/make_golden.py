@@ -1,10 +1,10 @@
 """Generate the golden fixtures by running the REFERENCE oracle itself.
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH   (or RAGGED_MLIR_REFERENCE=PATH)
 
 Imports ``oracle/reference.py`` and ``bench/distributions.py`` of the
-reference checkout (simon-jd/ragged-mlir; default /root/reference, only
-present in the build container) and writes ``golden.npz`` +
+reference checkout (simon-jd/ragged-mlir) named by --reference or the
+RAGGED_MLIR_REFERENCE environment variable and writes ``golden.npz`` +
 ``golden.json`` next to this script.  Each case holds its inputs (values as
 f32, already bf16-quantized for bf16 cases; offsets) and the reference's
 float64 outputs for sum, max and softmax.  The cases restate the
@@ -15,6 +15,7 @@ reference's own length generators (bench/distributions.py:15-64).
 from __future__ import annotations
 
 import argparse
+import os
 import json
 from pathlib import Path
 import sys
@@ -77,8 +78,11 @@ def cases(reference_bench):
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("RAGGED_MLIR_REFERENCE"),
+                        help="path of the reference checkout (default: $RAGGED_MLIR_REFERENCE)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("name the reference checkout with --reference or RAGGED_MLIR_REFERENCE")
     sys.path.insert(0, args.reference)
     from oracle import reference as ref  # the reference's own oracle
     from bench import distributions as dist  # the reference's own generators

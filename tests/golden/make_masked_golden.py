@@ -1,10 +1,10 @@
 """Generate the scale / mask golden fixtures by running the REFERENCE oracle.
 
-    python tests/golden/make_masked_golden.py [--reference PATH]
+    python tests/golden/make_masked_golden.py --reference PATH   (or RAGGED_MLIR_REFERENCE=PATH)
 
 Imports ``oracle/masked.py`` and ``oracle/reference.py`` of the reference
-checkout (simon-jd/ragged-mlir; default /root/reference, only present in the
-build container) and writes ``masked.npz`` + ``masked.json`` next to this
+checkout (simon-jd/ragged-mlir) named by --reference or the
+RAGGED_MLIR_REFERENCE environment variable and writes ``masked.npz`` + ``masked.json`` next to this
 script.  Each case holds its inputs (values as f32, already bf16-quantized
 for bf16 cases; the f32 mask; the scale; offsets), the reference's
 transformed logits (``masked_logits``) and its float64 softmax of them.  The
@@ -16,6 +16,7 @@ masks.
 from __future__ import annotations
 
 import argparse
+import os
 import json
 from pathlib import Path
 import sys
@@ -64,8 +65,11 @@ def cases():
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("RAGGED_MLIR_REFERENCE"),
+                        help="path of the reference checkout (default: $RAGGED_MLIR_REFERENCE)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("name the reference checkout with --reference or RAGGED_MLIR_REFERENCE")
     sys.path.insert(0, args.reference)
     from oracle import masked as ref_masked  # the reference's own oracle
     from oracle import reference as ref

@@ -171,8 +171,19 @@ def host(monkeypatch, tmp_path, native_library):
             log.append(("copy", source.numel() * 8))
             return self
 
+        def narrow(self, dim, start, length):
+            assert dim == 0 and self.dtype == "u8" and self.ndim == 1 and start + length <= self.shape[0]
+            return Tensor((length,), "u8", self.pointer + start, self.device)
+
+        def view(self, dtype):
+            assert self.dtype == "u8" and self.shape[0] % sizes[dtype] == 0
+            return Tensor((self.shape[0] // sizes[dtype],), dtype, self.pointer, self.device)
+
         def tolist(self):
             assert self.device == "cpu" and state["synchronized"]
+            if self.shape == (1,):  # the device status word read after the call
+                log.append(("read_device_word",))
+                return [state["device_word"]]
             log.append(("read_host_status",))
             return list(state["status"])
 
@@ -198,8 +209,9 @@ def host(monkeypatch, tmp_path, native_library):
 
     def run(*args):
         log.append(("launch", "main", args[-2] if len(args) > 1 else None))
+        state["synchronized"] = False
         return SimpleNamespace(num_launches=1, kernel_ids=[2], grid=[(4, 1, 1)], d_vector=1, d_tile=1, streams=1,
-                               thresholds=[0, 0])
+                               thresholds=[0, 0], status_offset=state.get("status_offset", -1))
 
     monkeypatch.setattr(runtime, "_torch", lambda: fake_torch)
     monkeypatch.setattr(runtime, "device_l2_mib", lambda _: 126.0, raising=False)
@@ -275,3 +287,31 @@ def test_zero_batch_with_rows_is_reported_by_the_device(host):
     assert caught.value.errors == {"final_mismatch": 0}
     with pytest.raises(ValidationError, match="B=0 requires N=0"):
         host.call(b=0, n=1, mode="validated")
+
+
+def test_checked_reads_the_device_status_word_after_the_call(host):
+    """A schedule that keeps a device status word (the classified worker's
+    bounded waits) reports its offset in the scratch; checked mode copies
+    the 8-byte word back after the main launch, on the execution stream."""
+    host.state["status_offset"] = 16
+    host.state["device_word"] = 0
+    host.call(select="classified")
+    kinds = _kinds(host.log)
+    main = next(i for i, event in enumerate(host.log) if event[:2] == ("launch", "main"))
+    assert [event for event in host.log if event[0] == "copy"] == [("copy", 56), ("copy", 8)]
+    assert kinds.index("read_device_word") > main
+    assert [event for event in host.log if event[0] == "synchronize"] == [("synchronize", 202)] * 2
+
+
+def test_checked_raises_when_a_bounded_wait_gave_up(host):
+    host.state["status_offset"] = 16
+    host.state["device_word"] = 1
+    with pytest.raises(RuntimeError, match="bounded wait"):
+        host.call(select="classified")
+
+
+def test_validated_mode_never_reads_the_device_status_word(host):
+    host.state["status_offset"] = 16
+    host.state["device_word"] = 1
+    host.call(mode="validated", select="classified")
+    assert not {"copy", "synchronize", "read_device_word"} & set(_kinds(host.log))

@@ -293,3 +293,22 @@ def test_classified_chunks_grow_for_giant_segments(cuda, op, rows):
     assert report.thresholds[0] == 32 and 32 < report.thresholds[1] <= 4096
     assert rows > 1024 * report.thresholds[1]
     check(actual, values, offsets, op, "bf16")
+
+
+@pytest.mark.parametrize("lengths", [[1, 7, 33, 300, 5000], [2, 64, 2, 900, 0, 3]])
+def test_f32_softmax_terms_far_below_the_maximum(cuda, lengths):
+    """f32 softmax with every logit but one per column 60 to 87 below the
+    column's maximum: the exponential's relative error (about |t| * 2^-23,
+    from rounding t = x - m and t * log2 e once each) reaches its largest
+    there, next to the 1e-5 bound; outputs near FLT_MIN test the flush
+    allowance.  Every schedule must stay within both contracts."""
+    rng = np.random.default_rng(6087)
+    lengths = np.array(lengths, dtype=np.int64)
+    offsets = offsets_of(lengths)
+    n = int(offsets[-1])
+    values = rng.uniform(-87.0, -60.0, size=(n, 32)).astype(np.float32) + np.float32(12.5)
+    for start, length in zip(offsets[:-1], lengths):
+        if length:
+            top = start + rng.integers(0, length, size=32)
+            values[top, np.arange(32)] = np.float32(12.5)
+    _run_all(cuda, "softmax", "f32", values, offsets)

@@ -162,3 +162,13 @@ def test_full_size_workloads_match_configuration():
     c5 = workloads.make("c5")
     assert c5.n == 200_000_000 and c5.b == 4_000_000 and c5.lengths.max() == 50_000_000
     assert int((c5.lengths > c5.n // 8).sum()) == 3
+
+
+def test_report_says_which_optimisation_controls_had_an_effect():
+    effects = Optimizations(shuffle=False, feature_tile=8).effects()
+    assert effects["applied"] == ["classification", "vectorize"]
+    assert {"shuffle", "online_fusion", "warp_mapping", "feature_tile", "pointwise_fusion"} <= set(effects["no_effect"])
+    assert "pointwise_fusion" in Optimizations().effects(transformed=True)["applied"]
+    every = set(effects["applied"]) | set(effects["no_effect"])
+    assert every == {"classification", "online_fusion", "warp_mapping", "split_mapping", "shuffle",
+                     "pointwise_fusion", "row_pipelining", "vectorize", "feature_tile"}
