@@ -65,6 +65,11 @@ enum rg_schedule {
  * statistics reads before it writes any of the segment's rows, and writes
  * each element only after its last read. */
 #define RG_FLAG_IN_PLACE 2u
+/* rg_run_pointwise: always materialise the transformed f32 logits (the
+ * reference's Optimizations(pointwise_fusion=False) route).  Without it, a
+ * softmax on the classified schedule whose rows the worker stages applies
+ * the transform as it loads. */
+#define RG_FLAG_NO_POINTWISE_FUSION 4u
 
 #define RG_MAX_LAUNCHES 8
 
@@ -137,11 +142,17 @@ int rg_run(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
  * docs/mask-abi.md; python/ragged/runtime.py:346-356 for the mask rules):
  * every value becomes x = f32(values) * scale (scale != 1) + mask (f32
  * [N][D], softmax only; NULL = none), two f32 roundings, and `op` runs on x
- * with `schedule`.  The transformed values are materialised in `workspace`
- * (the reference's route with pointwise fusion off, lib/Conversion/
- * ToGPU.cpp:41-60, 604-618); results round once to `dtype`.  The mask may
- * alias values but not out or offsets.  Workspace from
- * rg_pointwise_workspace_bytes; otherwise as rg_run. */
+ * with `schedule`; results round once to `dtype`.  A softmax on the
+ * classified schedule whose rows the worker stages (one column tile of
+ * 16-byte vectors; a mask 16-byte aligned and, in place, disjoint from
+ * values) applies the transform as it loads, as the reference's
+ * loadInput does (lib/Conversion/ToGPU.cpp:604-618); every other call, and
+ * any call with RG_FLAG_NO_POINTWISE_FUSION, materialises the transformed
+ * values in `workspace` first (the reference's route with pointwise fusion
+ * off, ToGPU.cpp:41-60).  rg_report.kernel_ids show which route ran.  The
+ * mask may alias values but not out or offsets.  Workspace from
+ * rg_pointwise_workspace_bytes (enough for either route); otherwise as
+ * rg_run. */
 int rg_pointwise_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
                                  int schedule, int64_t max_len, uint32_t flags, int64_t *bytes);
 int rg_run_pointwise(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,

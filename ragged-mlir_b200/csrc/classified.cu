@@ -144,8 +144,11 @@ int blocks_per_sm(const void *kernel, int device, int threads, int smem, int *bl
   return RG_OK;
 }
 
-template <typename T, typename OffT, int OP, int VEC, bool STAGED>
-int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t stream, rg_report *report) {
+// XF (softmax, staged rows only): the input transform `xf` fused into the
+// worker's and the normalise kernel's loads.
+template <typename T, typename OffT, int OP, int VEC, bool STAGED, bool XF = false>
+int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t stream, rg_report *report,
+                 const Xform &xf = Xform{}) {
   DeviceProps dev;
   int status = device_props(&dev);
   if (status) return status;
@@ -168,6 +171,7 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
   a.wait_rows = 0;
   a.late = reinterpret_cast<unsigned *>(ws + l.late);
   a.wait_polls = chunk_wait_polls();
+  a.xform = xf;
 
   // The pipelined worker's grid (one resident wave).  Softmax split segments
   // of at most min(kWaitChunks, ctas / 2) chunks are normalised by the
@@ -178,7 +182,7 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
   int64_t pipe_ctas = 0;
   if constexpr (STAGED) {
     using PL = PipeLayout<OP, VEC>;
-    const void *worker = reinterpret_cast<const void *>(&pipe_worker_kernel<T, OffT, OP, VEC>);
+    const void *worker = reinterpret_cast<const void *>(&pipe_worker_kernel<T, OffT, OP, VEC, XF>);
     status = blocks_per_sm(worker, dev.device, kPipeThreads, PL::kTotalBytes, &per_sm);
     if (status) return status;
     pipe_ctas = static_cast<int64_t>(per_sm) * dev.sm_count;
@@ -210,7 +214,7 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
   if constexpr (STAGED) {
     using PL = PipeLayout<OP, VEC>;
     dim3 wgrid(static_cast<unsigned>(pipe_ctas), 1, 1);
-    pipe_worker_kernel<T, OffT, OP, VEC><<<wgrid, kPipeThreads, PL::kTotalBytes, stream>>>(
+    pipe_worker_kernel<T, OffT, OP, VEC, XF><<<wgrid, kPipeThreads, PL::kTotalBytes, stream>>>(
         static_cast<const T *>(p.values), offsets, static_cast<T *>(p.out), a);
     record_launch(report, K_WORKER, wgrid, kPipeThreads, PL::kTotalBytes);
     status = check_cuda(cudaGetLastError(), "pipe_worker_kernel launch");
@@ -232,7 +236,7 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
 
   if constexpr (OP == OP_SOFTMAX) {
     if (l.splits > 0) {
-      const void *norm = reinterpret_cast<const void *>(&split_normalize_kernel<T, OffT, VEC>);
+      const void *norm = reinterpret_cast<const void *>(&split_normalize_kernel<T, OffT, VEC, XF>);
       status = blocks_per_sm(norm, dev.device, kClsThreads, 0, &per_sm);
       if (status) return status;
       int64_t nctas = static_cast<int64_t>(per_sm) * dev.sm_count;
@@ -240,7 +244,7 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
       if (nctas > (warps_needed + kClsWarps - 1) / kClsWarps) nctas = (warps_needed + kClsWarps - 1) / kClsWarps;
       if (nctas < 1) nctas = 1;
       dim3 ngrid(static_cast<unsigned>(nctas), 1, 1);
-      split_normalize_kernel<T, OffT, VEC><<<ngrid, kClsThreads, 0, stream>>>(
+      split_normalize_kernel<T, OffT, VEC, XF><<<ngrid, kClsThreads, 0, stream>>>(
           static_cast<const T *>(p.values), offsets, static_cast<T *>(p.out), a);
       record_launch(report, K_SPLIT_NORMALIZE, ngrid, kClsThreads, 0);
       status = check_cuda(cudaGetLastError(), "split_normalize_kernel launch");
@@ -286,7 +290,37 @@ int launch_index(const Problem &p, const Geometry &g, char *ws, cudaStream_t s, 
                                        : launch_op<T, int64_t>(p, g, ws, s, r);
 }
 
+template <typename T, typename OffT>
+int launch_fused_index(const Problem &p, const Geometry &g, char *ws, cudaStream_t s, rg_report *r,
+                       const Xform &xf) {
+  constexpr int VEC = 16 / static_cast<int>(sizeof(T));
+  return launch_typed<T, OffT, OP_SOFTMAX, VEC, true, true>(p, g, ws, s, r, xf);
+}
+
 }  // namespace
+
+bool classified_fuses(const Problem &p, const Geometry &g) {
+  return p.op == RG_OP_SOFTMAX && !(p.flags & RG_FLAG_NO_VECTORIZE) && staged_of(p, g);
+}
+
+int launch_classified_fused(const Problem &p, const Geometry &g, void *workspace, const float *mask, float scale,
+                            cudaStream_t stream, rg_report *report) {
+  if (!classified_fuses(p, g)) return fail(RG_ERR_UNSUPPORTED, "fused transform needs staged softmax rows");
+  if (p.b == 0) return RG_OK;
+  if (report) {
+    report->thresholds[0] = kWarpClassMax;
+    report->thresholds[1] = item_rows_of(p, g);
+    report->status_offset = static_cast<int64_t>(offsetof(ClsState, error));
+  }
+  const Xform xf{mask, p.d, scale, scale != 1.0f ? 1 : 0};
+  char *ws = static_cast<char *>(workspace);
+  const bool i32 = p.index_dtype == RG_INDEX_I32;
+  if (p.dtype == RG_DTYPE_F32)
+    return i32 ? launch_fused_index<float, int32_t>(p, g, ws, stream, report, xf)
+               : launch_fused_index<float, int64_t>(p, g, ws, stream, report, xf);
+  return i32 ? launch_fused_index<__nv_bfloat16, int32_t>(p, g, ws, stream, report, xf)
+             : launch_fused_index<__nv_bfloat16, int64_t>(p, g, ws, stream, report, xf);
+}
 
 int classified_workspace(const Problem &p, const Geometry &g, int64_t *bytes) {
   *bytes = p.b == 0 ? 0 : layout_of(p, g).total;

@@ -263,6 +263,7 @@ struct ClsArgs {
   int64_t wait_rows;   // softmax split segments up to this length are normalised by the worker (0: none)
   unsigned *late;      // softmax: [chunks] nonzero = chunk whose wait gave up (normalised by split_normalize)
   int wait_polls;      // polls before a wait gives up
+  Xform xform;         // softmax input transform fused into the loads (pipelined worker, normalise kernel)
 };
 
 // Worker of the classified schedule for rows that cannot be staged by bulk
@@ -411,8 +412,9 @@ cls_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets
 // statically over the warps in reverse chunk order, so the chunks the
 // worker read last are re-read first, from L2.  A warp finds its chunk's
 // split entry with a 32-ary search of split_base (three steps for 32K
-// split segments) and keeps 8 rows per lane group in flight.
-template <typename T, typename OffT, int VEC>
+// split segments) and keeps 8 rows per lane group in flight.  XF: the
+// softmax input transform (a.xform) is applied as rows are loaded.
+template <typename T, typename OffT, int VEC, bool XF = false>
 __global__ void __launch_bounds__(kClsThreads, 2)
 split_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
                        ClsArgs a) {
@@ -466,12 +468,19 @@ split_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ of
     int64_t r = r0 + q;
     for (; r + (U - 1) * step < r1; r += U * step) {
       Raw raw[U];
+      MaskVec<VEC> mk[U];
 #pragma unroll
-      for (int t = 0; t < U; ++t) raw[t] = VecIO<T, VEC>::load_raw(values + (r + t * step) * a.d + col);
+      for (int t = 0; t < U; ++t) {
+        raw[t] = VecIO<T, VEC>::load_raw(values + (r + t * step) * a.d + col);
+        if constexpr (XF) {
+          if (a.xform.mask) mk[t] = load_mask<VEC>(a.xform, r + t * step, col);
+        }
+      }
 #pragma unroll
       for (int t = 0; t < U; ++t) {
         float x[VEC], y[VEC];
         VecIO<T, VEC>::unpack(raw[t], x);
+        if constexpr (XF) apply_xform<VEC>(x, a.xform, mk[t]);
         normalize_vec<VEC>(x, y, ref, inv);
         VecIO<T, VEC>::store(out + (r + t * step) * a.d + col, y);
       }
@@ -479,6 +488,11 @@ split_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ of
     for (; r < r1; r += step) {
       float x[VEC], y[VEC];
       VecIO<T, VEC>::unpack(VecIO<T, VEC>::load_raw(values + r * a.d + col), x);
+      if constexpr (XF) {
+        MaskVec<VEC> mk;
+        if (a.xform.mask) mk = load_mask<VEC>(a.xform, r, col);
+        apply_xform<VEC>(x, a.xform, mk);
+      }
       normalize_vec<VEC>(x, y, ref, inv);
       VecIO<T, VEC>::store(out + r * a.d + col, y);
     }

@@ -510,4 +510,66 @@ struct Acc<OP_SOFTMAX, VEC> {
   }
 };
 
+// ------------------------------------------------------ input transform --
+
+// The reference's input transform (ProgramSpec scale and additive softmax
+// mask; its lib/Conversion/ToGPU.cpp:604-618 loadInput) applied as rows
+// are loaded: x = f32(v), then x * scale when scaled, then + mask, each
+// rounded to f32 with no fused multiply-add, so the results equal those of
+// a schedule run on materialised f32 logits.  `mask` (f32 [N][D], 16-byte
+// aligned rows) is null when there is none.
+struct Xform {
+  const float *mask;
+  int64_t d;
+  float scale;
+  int scaled;
+};
+
+// This thread's mask vector of row r (VEC floats from column col), loaded
+// in pieces of up to 16 bytes (the mask rows are aligned to VEC floats).
+template <int VEC>
+struct MaskVec {
+  using Piece = typename std::conditional<VEC % 4 == 0, float4,
+                                          typename std::conditional<VEC % 2 == 0, float2, float>::type>::type;
+  static constexpr int kPer = sizeof(Piece) / 4;
+  Piece part[VEC / kPer];
+  __device__ __forceinline__ float get(int v) const {
+    const Piece &p = part[v / kPer];
+    if constexpr (kPer == 4) {
+      switch (v % 4) {
+        case 0: return p.x;
+        case 1: return p.y;
+        case 2: return p.z;
+        default: return p.w;
+      }
+    } else if constexpr (kPer == 2) {
+      return v % 2 == 0 ? p.x : p.y;
+    } else {
+      return p;
+    }
+  }
+};
+
+template <int VEC>
+__device__ __forceinline__ MaskVec<VEC> load_mask(const Xform &xf, int64_t r, int64_t col) {
+  using M = MaskVec<VEC>;
+  M m;
+  const typename M::Piece *p = reinterpret_cast<const typename M::Piece *>(xf.mask + r * xf.d + col);
+#pragma unroll
+  for (int i = 0; i < VEC / M::kPer; ++i) m.part[i] = __ldg(p + i);
+  return m;
+}
+
+template <int VEC>
+__device__ __forceinline__ void apply_xform(float (&x)[VEC], const Xform &xf, const MaskVec<VEC> &m) {
+  if (xf.scaled) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) x[v] = __fmul_rn(x[v], xf.scale);
+  }
+  if (xf.mask) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) x[v] = __fadd_rn(x[v], m.get(v));
+  }
+}
+
 }  // namespace rgb

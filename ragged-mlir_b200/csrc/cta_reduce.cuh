@@ -223,16 +223,59 @@ __device__ __forceinline__ typename VecIO<T, VEC>::Raw pack_raw(const float (&y)
 // `base`.  Keeping the terms halves the SFU work of a staged softmax; for
 // bf16 output the extra rounding keeps the result within one ulp of the
 // rounded exact value (a half-ulp error on e, then the final rounding).
-template <typename T, int VEC>
+template <typename T, int VEC, bool XF = false>
 __device__ __forceinline__ void staged_stats_keep(Acc<OP_SOFTMAX, VEC> &acc, const SharedRows<T, VEC> &src,
                                                   int64_t begin, int64_t end, int64_t row_lane, int64_t step,
-                                                  float (&base)[VEC]) {
+                                                  float (&base)[VEC], const Xform &xf = Xform{}, int64_t col = 0) {
   constexpr int U = kFoldUnroll;
   using Raw = typename VecIO<T, VEC>::Raw;
   static_assert(VEC % 2 == 0, "packed pairs");
   constexpr int P = VEC / 2;
   float m[VEC], s[VEC];
-  rows_max<T, VEC>(m, src, begin, end, row_lane, step);
+  const int count = lane_rows(begin, end, row_lane, step);
+  const auto cur = src.at(begin + row_lane, step);
+  const int64_t row = begin + row_lane;  // whole-array row of this thread's k = 0 (the mask's row)
+  if (XF && !xf.mask && xf.scaled && xf.scale > 0.0f) {
+    // A positive scale keeps the order and rounding is monotone, so the
+    // maximum of the scaled values is the scaled maximum (NaN and infinities
+    // included): the packed maximum of the stored values, scaled once.
+    rows_max<T, VEC>(m, src, begin, end, row_lane, step);
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) m[v] = __fmul_rn(m[v], xf.scale);
+  } else if constexpr (XF) {
+    // Transformed maximum: f32 arithmetic (a mask or scale leaves the bf16 grid).
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) m[v] = -kInf;
+    int k = 0;
+    for (; k + U <= count; k += U) {
+      Raw raw[U];
+      MaskVec<VEC> mk[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        raw[u] = cur.raw(k + u);
+        if (xf.mask) mk[u] = load_mask<VEC>(xf, row + (k + u) * step, col);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float x[VEC];
+        VecIO<T, VEC>::unpack(raw[u], x);
+        apply_xform<VEC>(x, xf, mk[u]);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], x[v]);
+      }
+    }
+    for (; k < count; ++k) {
+      float x[VEC];
+      MaskVec<VEC> mk;
+      if (xf.mask) mk = load_mask<VEC>(xf, row + k * step, col);
+      VecIO<T, VEC>::unpack(cur.raw(k), x);
+      apply_xform<VEC>(x, xf, mk);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], x[v]);
+    }
+  } else {
+    rows_max<T, VEC>(m, src, begin, end, row_lane, step);
+  }
 #pragma unroll
   for (int v = 0; v < VEC; ++v) base[v] = m[v] == -kInf ? 0.0f : m[v];  // all -inf: every term is e^-inf = 0
   unsigned long long b2[P], s2[P];
@@ -241,11 +284,10 @@ __device__ __forceinline__ void staged_stats_keep(Acc<OP_SOFTMAX, VEC> &acc, con
     b2[k] = pack2(base[2 * k], base[2 * k + 1]);
     s2[k] = pack2(0.0f, 0.0f);
   }
-  const int count = lane_rows(begin, end, row_lane, step);
-  const auto cur = src.at(begin + row_lane, step);
-  auto keep_row = [&](const Raw &raw, int k) {
+  auto keep_row = [&](const Raw &raw, const MaskVec<VEC> &mk, int k) {
     float x[VEC], e[VEC];
     VecIO<T, VEC>::unpack(raw, x);
+    if constexpr (XF) apply_xform<VEC>(x, xf, mk);
 #pragma unroll
     for (int j = 0; j < P; ++j) {
       const unsigned long long t = exp_diff2(pack2(x[2 * j], x[2 * j + 1]), b2[j]);
@@ -257,12 +299,24 @@ __device__ __forceinline__ void staged_stats_keep(Acc<OP_SOFTMAX, VEC> &acc, con
   int k = 0;
   for (; k + U <= count; k += U) {
     Raw raw[U];
+    MaskVec<VEC> mk[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) raw[u] = cur.raw(k + u);
+    for (int u = 0; u < U; ++u) {
+      raw[u] = cur.raw(k + u);
+      if constexpr (XF) {
+        if (xf.mask) mk[u] = load_mask<VEC>(xf, row + (k + u) * step, col);
+      }
+    }
 #pragma unroll
-    for (int u = 0; u < U; ++u) keep_row(raw[u], k + u);
+    for (int u = 0; u < U; ++u) keep_row(raw[u], mk[u], k + u);
   }
-  for (; k < count; ++k) keep_row(cur.raw(k), k);
+  for (; k < count; ++k) {
+    MaskVec<VEC> mk;
+    if constexpr (XF) {
+      if (xf.mask) mk = load_mask<VEC>(xf, row + k * step, col);
+    }
+    keep_row(cur.raw(k), mk, k);
+  }
 #pragma unroll
   for (int j = 0; j < P; ++j) unpack2(s2[j], s[2 * j], s[2 * j + 1]);
 #pragma unroll

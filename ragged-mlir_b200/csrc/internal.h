@@ -80,6 +80,16 @@ int launch_rowbal(const Problem &p, const Geometry &g, void *workspace, cudaStre
 // Resident CTAs per SM of a row-balanced kernel, cached per (kernel, device).
 int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks);
 int classified_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
+// Softmax on the classified schedule with the input transform (scale,
+// additive mask) fused into the loads: for rows the pipelined worker stages.
+bool classified_fuses(const Problem &p, const Geometry &g);
+int launch_classified_fused(const Problem &p, const Geometry &g, void *workspace, const float *mask, float scale,
+                            cudaStream_t stream, rg_report *report);
+// Softmax on the row-balanced schedule with the transform fused into both
+// passes' loads (the workspace is rowbal_workspace's).
+bool rowbal_fuses(const Problem &p, const Geometry &g, const float *mask);
+int launch_rowbal_fused(const Problem &p, const Geometry &g, void *workspace, const float *mask, float scale,
+                        cudaStream_t stream, rg_report *report);
 int launch_classified(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
 
 // Any schedule: its scratch bytes, and its launch for a validated problem.

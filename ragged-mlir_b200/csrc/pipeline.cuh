@@ -148,10 +148,11 @@ __device__ __forceinline__ void fold_staged(Acc<OP, VEC> &acc, const Src &src, i
   }
 }
 
-template <typename T, typename OffT, int OP, int VEC>
 #ifndef RG_PIPE_MIN_BLOCKS
 #define RG_PIPE_MIN_BLOCKS 1
 #endif
+// XF: softmax with the input transform fused into the loads (a.xform).
+template <typename T, typename OffT, int OP, int VEC, bool XF = false>
 __global__ void __launch_bounds__(kPipeThreads, RG_PIPE_MIN_BLOCKS)
 pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out, ClsArgs a) {
   using L = PipeLayout<OP, VEC>;
@@ -391,7 +392,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
             // The mass pass keeps its terms in the stage; the normalisation
             // scales them by e^(base - M) / total.
             float base[VEC], mine[VEC];
-            if (active) staged_stats_keep<T, VEC>(acc, rows, begin, end, q, warp_step, base);
+            if (active) staged_stats_keep<T, VEC, XF>(acc, rows, begin, end, q, warp_step, base, a.xform, col);
 #pragma unroll
             for (int v = 0; v < VEC; ++v) mine[v] = acc.st[v].r;
             warp_merge<OP, VEC>(acc, G);
@@ -422,7 +423,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       if (active) {
         if constexpr (OP == OP_SOFTMAX) {
           Acc<OP, VEC> stage_acc;
-          staged_stats_keep<T, VEC>(stage_acc, rows, r.r0, r.r1, team_lane, team_step, base);
+          staged_stats_keep<T, VEC, XF>(stage_acc, rows, r.r0, r.r1, team_lane, team_step, base, a.xform, col);
 #pragma unroll
           for (int v = 0; v < VEC; ++v) mine[v] = stage_acc.st[v].r;
           split_acc.merge(stage_acc);

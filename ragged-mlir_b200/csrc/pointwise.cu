@@ -124,6 +124,40 @@ int layout_of(const Problem &p, int schedule, PointwiseLayout *l) {
   return RG_OK;
 }
 
+// How a call runs its transform.  Fused routes (softmax only, fusion not
+// switched off, not in place over values a mask aliases):
+//   row-balanced schedule  the statistics and normalise passes read values
+//                          and mask together (mask rows aligned to the
+//                          call's vector width);
+//   classified schedule    with staged rows and a scale but no mask: the
+//                          worker scales rows as it reads them from shared
+//                          memory.  (With a mask the worker would wait on
+//                          global mask loads between shared-memory passes;
+//                          measured on B200 that is slower than the
+//                          materialised route, so a mask goes there.)
+// Everything else materialises the transformed f32 logits first.
+enum Route { MATERIALIZED = 0, FUSED_ROWBAL = 1, FUSED_CLASSIFIED = 2 };
+
+int route_of(const Problem &p, const Geometry &g, int schedule, const float *mask) {
+  if (p.op != RG_OP_SOFTMAX || (p.flags & RG_FLAG_NO_POINTWISE_FUSION)) return MATERIALIZED;
+  if (mask && (p.flags & RG_FLAG_IN_PLACE)) {
+    const uintptr_t mb = reinterpret_cast<uintptr_t>(mask), me = mb + p.n * p.d * 4;
+    const uintptr_t vb = reinterpret_cast<uintptr_t>(p.values), ve = vb + p.n * p.d * elem_bytes(p.dtype);
+    if (mb < ve && vb < me) return MATERIALIZED;
+  }
+  if (schedule == RG_SCHEDULE_ROWBALANCED && rowbal_fuses(p, g, mask)) return FUSED_ROWBAL;
+  if (schedule == RG_SCHEDULE_CLASSIFIED && !mask && classified_fuses(p, g)) return FUSED_CLASSIFIED;
+  return MATERIALIZED;
+}
+
+// Scratch of a fused route (the schedule's own workspace for the original problem).
+int fused_workspace(const Problem &p, const Geometry &g, int route, int64_t *bytes) {
+  *bytes = 0;
+  if (route == FUSED_ROWBAL) return rowbal_workspace(p, g, bytes);
+  if (route == FUSED_CLASSIFIED) return classified_workspace(p, g, bytes);
+  return RG_OK;
+}
+
 int grid_for(int64_t items, const DeviceProps &dev) {
   int64_t blocks = (items + kPointwiseThreads - 1) / kPointwiseThreads;
   const int64_t cap = static_cast<int64_t>(dev.sm_count) * 8;
@@ -195,6 +229,17 @@ int rg_pointwise_workspace_bytes(int op, int dtype, int index_dtype, int64_t d, 
   status = layout_of(p, schedule, &l);
   if (status) return status;
   *bytes = l.total;
+  // Enough for a fused route too (which route runs depends on the mask pointer).
+  const Geometry g = make_geometry(p);
+  for (int route : {FUSED_ROWBAL, FUSED_CLASSIFIED}) {
+    const bool possible = route == FUSED_ROWBAL ? schedule == RG_SCHEDULE_ROWBALANCED && op == RG_OP_SOFTMAX
+                                                : schedule == RG_SCHEDULE_CLASSIFIED && classified_fuses(p, g);
+    if (!possible) continue;
+    int64_t fused = 0;
+    status = fused_workspace(p, g, route, &fused);
+    if (status) return status;
+    if (fused > *bytes) *bytes = fused;
+  }
   return RG_OK;
 }
 
@@ -228,6 +273,23 @@ int rg_run_pointwise(int op, int dtype, int index_dtype, int64_t d, int64_t n, i
   DeviceProps dev;
   status = check_device(&dev);
   if (status) return status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const Geometry g0 = make_geometry(p);
+  const int route = route_of(p, g0, schedule, mask);
+  if (route != MATERIALIZED) {
+    int64_t need = 0;
+    status = fused_workspace(p, g0, route, &need);
+    if (status) return status;
+    if (report) {
+      report->workspace_bytes = need;
+      report->d_vector = g0.vec;
+      report->d_tile = 1 << g0.g_shift;
+    }
+    if (!workspace || workspace_bytes < need) return fail(RG_ERR_WORKSPACE, "workspace missing or too small");
+    if (!aligned(workspace, 256)) return fail(RG_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    return route == FUSED_ROWBAL ? launch_rowbal_fused(p, g0, workspace, mask, scale, s, report)
+                                 : launch_classified_fused(p, g0, workspace, mask, scale, s, report);
+  }
   PointwiseLayout l;
   status = layout_of(p, schedule, &l);
   if (status) return status;
@@ -238,7 +300,6 @@ int rg_run_pointwise(int op, int dtype, int index_dtype, int64_t d, int64_t n, i
   float *logits = reinterpret_cast<float *>(ws);
   float *results = dtype == RG_DTYPE_F32 ? static_cast<float *>(out)
                                          : (op == RG_OP_SOFTMAX ? logits : reinterpret_cast<float *>(ws + l.logits_bytes));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   status = dtype == RG_DTYPE_F32 ? launch_logits<float>(p, mask, scale, logits, dev, s, report)
                                  : launch_logits<__nv_bfloat16>(p, mask, scale, logits, dev, s, report);
   if (status) return status;

@@ -38,10 +38,10 @@ namespace {
 // statistics (3 floats per feature) get the registers of 2.
 constexpr int minb_of(int op) { return op == OP_SOFTMAX ? 2 : RowbalTuning::kMinBlocks; }
 
-template <typename T, typename OffT, int OP, int VEC>
+template <typename T, typename OffT, int OP, int VEC, bool XF = false>
 const void *kernel_ptr() {
   return reinterpret_cast<const void *>(
-      &rowbal_kernel<T, OffT, OP, VEC, RowbalTuning::kUnroll, RowbalTuning::kDoubleBuffer, minb_of(OP)>);
+      &rowbal_kernel<T, OffT, OP, VEC, RowbalTuning::kUnroll, RowbalTuning::kDoubleBuffer, minb_of(OP), XF>);
 }
 
 // Narrow rows that pack whole rows into 16-byte packets (2, 4 or 8 bytes a
@@ -120,12 +120,15 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
   return RG_OK;
 }
 
-template <typename T, typename OffT, int OP, int VEC>
+// XF (softmax only): the input transform `xf` fused into the statistics and
+// normalise passes' loads.
+template <typename T, typename OffT, int OP, int VEC, bool XF = false>
 int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *bytes, cudaStream_t stream,
-              rg_report *report) {
+              rg_report *report, const Xform &xf = Xform{}) {
+  static_assert(!XF || OP == OP_SOFTMAX, "the fused transform is a softmax route");
   Plan plan;
-  const void *packed = packs(p, g) ? packed_ptr<T, OffT, OP, VEC>() : nullptr;
-  int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC>(), packed, &plan);
+  const void *packed = XF ? nullptr : (packs(p, g) ? packed_ptr<T, OffT, OP, VEC>() : nullptr);
+  int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC, XF>(), packed, &plan);
   if (status) return status;
   if (bytes) {
     *bytes = plan.stats + plan.stats_bytes;
@@ -164,10 +167,10 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   T *const target = OP == OP_SOFTMAX ? reinterpret_cast<T *>(static_cast<char *>(workspace) + plan.stats)
                                      : static_cast<T *>(p.out);
   dim3 grid(static_cast<unsigned>(plan.grid), g.col_tiles, 1);
-  rowbal_kernel<T, OffT, OP, VEC, RowbalTuning::kUnroll, RowbalTuning::kDoubleBuffer, minb_of(OP)>
+  rowbal_kernel<T, OffT, OP, VEC, RowbalTuning::kUnroll, RowbalTuning::kDoubleBuffer, minb_of(OP), XF>
       <<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), target, p.n, p.b,
-      p.d, g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{0, p.n, 1}, counter);
+      p.d, g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{0, p.n, 1}, counter, xf);
   record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch");
   if (status) return status;
@@ -186,9 +189,10 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
       const int64_t wanted = (p.n + 16 * units_per_cta - 1) / (16 * units_per_cta);  // >= 16 rows per unit
       if (ctas > wanted) ctas = wanted;
       dim3 ngrid(static_cast<unsigned>(ctas), g.col_tiles, 1);
-      rowbal_normalize_kernel<T, OffT, VEC><<<ngrid, kRowbalThreads, 0, stream>>>(
+      rowbal_normalize_kernel<T, OffT, VEC, 8, XF><<<ngrid, kRowbalThreads, 0, stream>>>(
           static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out),
-          reinterpret_cast<const float *>(target), p.n, p.b, p.d, g.g_shift, g.vec_cols, ctas * units_per_cta);
+          reinterpret_cast<const float *>(target), p.n, p.b, p.d, g.g_shift, g.vec_cols, ctas * units_per_cta,
+          0, 0, 0, xf);
       record_launch(report, K_ROWBAL_NORMALIZE, ngrid, kRowbalThreads, 0);
       status = check_cuda(cudaGetLastError(), "rowbal_normalize_kernel launch");
     }
@@ -230,7 +234,39 @@ int dispatch(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cuda
                                  : run_index<__nv_bfloat16>(p, g, ws, bytes, s, r);
 }
 
+template <typename T, typename OffT>
+int fused_vec(const Problem &p, const Geometry &g, void *ws, int64_t *bytes, cudaStream_t s, rg_report *r,
+              const Xform &xf) {
+  switch (g.vec) {
+    case 1: return run_typed<T, OffT, OP_SOFTMAX, 1, true>(p, g, ws, bytes, s, r, xf);
+    case 2: return run_typed<T, OffT, OP_SOFTMAX, 2, true>(p, g, ws, bytes, s, r, xf);
+    case 4: return run_typed<T, OffT, OP_SOFTMAX, 4, true>(p, g, ws, bytes, s, r, xf);
+    case 8:
+      if constexpr (sizeof(T) == 2) return run_typed<T, OffT, OP_SOFTMAX, 8, true>(p, g, ws, bytes, s, r, xf);
+      break;
+  }
+  return fail(RG_ERR_INVALID_ARGUMENT, "unsupported vector width");
+}
+
 }  // namespace
+
+bool rowbal_fuses(const Problem &p, const Geometry &, const float *mask) {
+  // The mask is read VEC floats at a time: its rows must be aligned to them.
+  const int vec = make_geometry(p).vec;
+  return p.op == RG_OP_SOFTMAX && (!mask || aligned(mask, 4 * vec));
+}
+
+int launch_rowbal_fused(const Problem &p, const Geometry &g, void *workspace, const float *mask, float scale,
+                        cudaStream_t stream, rg_report *report) {
+  if (p.b == 0) return RG_OK;
+  const Xform xf{mask, p.d, scale, scale != 1.0f ? 1 : 0};
+  const bool i32 = p.index_dtype == RG_INDEX_I32;
+  if (p.dtype == RG_DTYPE_F32)
+    return i32 ? fused_vec<float, int32_t>(p, g, workspace, nullptr, stream, report, xf)
+               : fused_vec<float, int64_t>(p, g, workspace, nullptr, stream, report, xf);
+  return i32 ? fused_vec<__nv_bfloat16, int32_t>(p, g, workspace, nullptr, stream, report, xf)
+             : fused_vec<__nv_bfloat16, int64_t>(p, g, workspace, nullptr, stream, report, xf);
+}
 
 int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes) {
   if (p.b == 0) {

@@ -343,13 +343,15 @@ __device__ __forceinline__ int64_t window_diag(const OffT *offsets, int64_t n, i
   return row + ends_upto(offsets, b, row, g, gl, group_mask, group_base);
 }
 
+// XF (softmax statistics, one GPU): the input transform `xf` (scale,
+// additive mask) applied to every row as it is loaded.
 template <typename T, typename OffT, int OP, int VEC, int U = RowbalTuning::kUnroll,
-          bool DB = RowbalTuning::kDoubleBuffer, int MINB = RowbalTuning::kMinBlocks>
+          bool DB = RowbalTuning::kDoubleBuffer, int MINB = RowbalTuning::kMinBlocks, bool XF = false>
 __global__ void __launch_bounds__(kRowbalThreads, MINB)
 rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
               int64_t n, int64_t b, int64_t d, int g_shift, int vec_cols, int64_t units,
               float *__restrict__ pieces, UnitMeta *__restrict__ meta, RowWindow window,
-              unsigned long long *__restrict__ work) {
+              unsigned long long *__restrict__ work, Xform xf = Xform{}) {
   using Acc = RowAcc<OP, VEC>;
   const int lane = threadIdx.x & 31;
   const int G = 1 << g_shift;
@@ -443,17 +445,27 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   // segment boundary takes the fast path (no per-row boundary test).
   using Raw = typename VecIO<T, VEC>::Raw;
   const T *ptr = values + (j0 - window.row0) * d + col;
+  MaskVec<VEC> mk[U];  // XF: the mask vectors of the batch's rows
   auto load_batch = [&](Raw (&raw)[U], int64_t rel) {  // rows j0 + rel .. + U
 #pragma unroll
     for (int t = 0; t < U; ++t)
-      if (active && j0 + rel + t < j1) raw[t] = VecIO<T, VEC>::load_raw(ptr + (rel + t) * d);
+      if (active && j0 + rel + t < j1) {
+        raw[t] = VecIO<T, VEC>::load_raw(ptr + (rel + t) * d);
+        if constexpr (XF) {
+          if (xf.mask) mk[t] = load_mask<VEC>(xf, j0 + rel + t, col);
+        }
+      }
+  };
+  auto unpack_row = [&](const Raw &raw, int t, float (&x)[VEC]) {
+    VecIO<T, VEC>::unpack(raw, x);
+    if constexpr (XF) apply_xform<VEC>(x, xf, mk[t]);
   };
   auto fold_batch = [&](const Raw (&raw)[U], int64_t r) {
     if (r + U <= j1 && next_b >= r + U) {
       if constexpr (OP == OP_SOFTMAX) {
         float x[U][VEC];
 #pragma unroll
-        for (int t = 0; t < U; ++t) VecIO<T, VEC>::unpack(raw[t], x[t]);
+        for (int t = 0; t < U; ++t) unpack_row(raw[t], t, x[t]);
         acc.template fold_batch<U>(x);  // one recentring test per batch and feature
       } else {
 #pragma unroll
@@ -470,7 +482,7 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
       // recentring test per piece instead of one per row.
       float x[U][VEC];
 #pragma unroll
-      for (int t = 0; t < U; ++t) VecIO<T, VEC>::unpack(raw[t], x[t]);
+      for (int t = 0; t < U; ++t) unpack_row(raw[t], t, x[t]);
       int t0 = 0;
       const int tn = j1 - r < U ? static_cast<int>(j1 - r) : U;
       while (t0 < tn) {
@@ -497,6 +509,7 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
       }
     }
   };
+  static_assert(!(XF && DB), "the fused transform keeps one batch of mask vectors");
   if constexpr (DB) {
     Raw ra[U], rb[U];
     load_batch(ra, 0);
@@ -941,11 +954,12 @@ __device__ __forceinline__ int64_t segment_before(const OffT *offsets, int64_t s
 // split evenly over the units (every row costs the same); each unit walks
 // its rows from the last to the first, so the rows the statistics pass read
 // last -- the ends of its units' slices -- are re-read while still in L2.
-template <typename T, typename OffT, int VEC, int U = 8>
+template <typename T, typename OffT, int VEC, int U = 8, bool XF = false>
 __global__ void __launch_bounds__(kRowbalThreads, 3)
 rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
                         const float *__restrict__ stats, int64_t n, int64_t b, int64_t d, int g_shift, int vec_cols,
-                        int64_t units, int64_t row_base = 0, int64_t seg0 = 0, int64_t seg1 = 0) {
+                        int64_t units, int64_t row_base = 0, int64_t seg0 = 0, int64_t seg1 = 0,
+                        Xform xf = Xform{}) {
   // values[i] and out[i] hold row row_base + i of the whole array (a rank's
   // window of a sharded call; 0 otherwise); the statistics of segment s sit
   // at slot s - seg0 (seg1: end of the slots, 0 = unbounded).
@@ -979,9 +993,10 @@ rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ o
   using Raw = typename VecIO<T, VEC>::Raw;
   const T *const src = values + col;  // row r sits at (r - row_base) * d
   T *const dst = out + col;
-  auto normalize_row = [&](const Raw &raw, int64_t r) {
+  auto normalize_row = [&](const Raw &raw, const MaskVec<VEC> &mk, int64_t r) {
     float x[VEC], y[VEC];
     VecIO<T, VEC>::unpack(raw, x);
+    if constexpr (XF) apply_xform<VEC>(x, xf, mk);
 #pragma unroll
     for (int v = 0; v < VEC; ++v) y[v] = stats_normalize(x[v], ref[v], inv[v]);
     VecIO<T, VEC>::store(dst + (r - row_base) * d, y);
@@ -989,9 +1004,15 @@ rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ o
   int64_t r = r1 - 1;
   for (; r - (U - 1) >= r0; r -= U) {
     Raw raw[U];
+    MaskVec<VEC> mk[U];
 #pragma unroll
     for (int t = 0; t < U; ++t)
-      if (active) raw[t] = VecIO<T, VEC>::load_raw(src + (r - t - row_base) * d);
+      if (active) {
+        raw[t] = VecIO<T, VEC>::load_raw(src + (r - t - row_base) * d);
+        if constexpr (XF) {
+          if (xf.mask) mk[t] = load_mask<VEC>(xf, r - t, col);
+        }
+      }
 #pragma unroll
     for (int t = 0; t < U; ++t) {
       if (r - t < start) {  // an earlier segment (skipping empty ones)
@@ -999,7 +1020,7 @@ rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ o
         start = load_offset(offsets, seg);
         if (active) load_stats();
       }
-      if (active) normalize_row(raw[t], r - t);
+      if (active) normalize_row(raw[t], mk[t], r - t);
     }
   }
   for (; r >= r0; --r) {
@@ -1008,7 +1029,13 @@ rowbal_normalize_kernel(const T *__restrict__ values, const OffT *__restrict__ o
       start = load_offset(offsets, seg);
       if (active) load_stats();
     }
-    if (active) normalize_row(VecIO<T, VEC>::load_raw(src + (r - row_base) * d), r);
+    if (active) {
+      MaskVec<VEC> mk;
+      if constexpr (XF) {
+        if (xf.mask) mk = load_mask<VEC>(xf, r, col);
+      }
+      normalize_row(VecIO<T, VEC>::load_raw(src + (r - row_base) * d), mk, r);
+    }
   }
 }
 

@@ -132,7 +132,8 @@ int shard_typed(const Problem &p, const Geometry &g, const ShardCall &c, void *w
   dim3 grid(static_cast<unsigned>(plan.grid), g.col_tiles, 1);
   shard_kernel<T, OffT, OP, VEC>()<<<grid, kRowbalThreads, kRowbalSmem, stream>>>(
       static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), target, p.n, p.b, p.d,
-      g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{c.row0, c.row1, c.first, seg0, seg1}, counter);
+      g.g_shift, g.vec_cols, units, pieces, meta, RowWindow{c.row0, c.row1, c.first, seg0, seg1}, counter,
+      Xform{});
   record_launch(report, K_ROWBAL, grid, kRowbalThreads, kRowbalSmem);
   status = check_cuda(cudaGetLastError(), "rowbal_kernel launch (shard)");
   if (status) return status;

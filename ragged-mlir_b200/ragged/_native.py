@@ -26,6 +26,7 @@ SCHEDULES = {"classified": 0, "naive": 1, "rowbalanced": 2}
 SCHEDULE_NAMES = {value: key for key, value in SCHEDULES.items()}
 FLAG_NO_VECTORIZE = 1
 FLAG_IN_PLACE = 2
+FLAG_NO_POINTWISE_FUSION = 4
 MAX_LAUNCHES = 8
 
 # Every symbol include/ragged_b200.h declares.

@@ -8,6 +8,9 @@ compiler passes only select among the built-in schedules:
 * ``classification=False`` makes a program use block-per-segment only;
 * ``vectorize=False`` makes every thread access one feature at a time
   (``RG_FLAG_NO_VECTORIZE``);
+* ``pointwise_fusion=False`` makes a scale or mask always go through
+  materialised f32 logits (``RG_FLAG_NO_POINTWISE_FUSION``); otherwise a
+  softmax on the classified schedule applies it as it loads;
 * the other flags are recorded in the report and otherwise have no effect.
 """
 from __future__ import annotations

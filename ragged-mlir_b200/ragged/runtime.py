@@ -99,8 +99,12 @@ class CompiledProgram:
         self._span = tile * vec
         self._flags = (0 if spec.optimizations.vectorize else _native.FLAG_NO_VECTORIZE) | (
             _native.FLAG_IN_PLACE if spec.alias == "inplace" else 0)
-        # Scale or mask: the transformed input is materialised (rg_run_pointwise).
+        # Scale or mask: rg_run_pointwise (fused into the classified worker's
+        # loads for staged softmax rows, else materialised; pointwise_fusion=False
+        # always materialises, the reference's route).
         self._pointwise = spec.mask or float(spec.scale) != 1.0
+        if self._pointwise and not spec.optimizations.pointwise_fusion:
+            self._flags |= _native.FLAG_NO_POINTWISE_FUSION
 
     @property
     def selects(self) -> bool:
@@ -450,5 +454,5 @@ class CompiledProgram:
                                validation_host_ms=validation_ms if validation is not None else None,
                                optimizations={"requested": self.spec.optimizations.to_dict(),
                                               **self.spec.optimizations.effects(transformed=self._pointwise)},
-                               pointwise_materialized=self._pointwise,
+                               pointwise_materialized=self._pointwise and "pointwise_logits" in names,
                                d_tile=tile, d_vector=vec, streams=streams, selected=schedule, selection=selection)

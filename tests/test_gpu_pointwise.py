@@ -1,6 +1,9 @@
 """The input transform on the GPU: ProgramSpec(scale=...) for every op and
 the additive f32 softmax mask (rg_run_pointwise), on every schedule, against
-the oracle's masked logits.  Restates the reference's test/gpu/test_mask.py:
+the oracle's masked logits.  Softmax on the classified schedule with staged
+rows applies the transform as it loads (fused); every other call goes
+through materialised f32 logits, as does every call of a program compiled
+with Optimizations(pointwise_fusion=False).  Restates the reference's test/gpu/test_mask.py:
 all schedules and widths, f32 mask cancellation, separate roundings,
 non-finite and fully masked columns, in place and checked calls, mask
 aliasing rules and invalid masks (output untouched), the custom op.
@@ -21,13 +24,31 @@ SCHEDULES = ("naive", "classified", "rowbalanced")
 
 
 @functools.lru_cache(maxsize=128)
-def pw_program(op, dtype, d, index="i64", mask=False, scale=1.0, inplace=False):
-    from ragged import ArtifactCache, Compiler, ProgramSpec
-    spec = ProgramSpec(op, dtype, d, index, mask=mask, scale=scale, alias="inplace" if inplace else "none")
+def pw_program(op, dtype, d, index="i64", mask=False, scale=1.0, inplace=False, fusion=True):
+    from ragged import ArtifactCache, Compiler, Optimizations, ProgramSpec
+    spec = ProgramSpec(op, dtype, d, index, mask=mask, scale=scale, alias="inplace" if inplace else "none",
+                       optimizations=Optimizations(pointwise_fusion=fusion))
     return Compiler().compile(spec, ArtifactCache(_cache_dir(), max_specializations=4096))
 
 
-def run_masked(torch, op, dtype, values, offsets, mask, scale, select, *, inplace=False, mode="validated"):
+def fused_expected(op, dtype, d, select, mask_ptr, inplace_alias=False, fusion=True):
+    """Whether rg_run_pointwise takes a fused route for this call: softmax on
+    the row-balanced schedule (mask rows aligned to the vector width), or on
+    the classified schedule with staged rows and no mask."""
+    if not fusion or op != "softmax" or inplace_alias:
+        return False
+    element = 2 if dtype == "bf16" else 4
+    vec = 1
+    while 2 * vec * element <= 16 and d % (2 * vec) == 0:
+        vec *= 2
+    if select == "rowbalanced":
+        return mask_ptr is None or mask_ptr % (4 * vec) == 0
+    staged = (dtype == "bf16" and d % 8 == 0 and d <= 256) or (dtype == "f32" and d % 4 == 0 and d <= 128)
+    return select == "classified" and staged and mask_ptr is None
+
+
+def run_masked(torch, op, dtype, values, offsets, mask, scale, select, *, inplace=False, mode="validated",
+               fusion=True):
     """(result as float64, report); guards around out and mask."""
     d = values.shape[1]
     tdtype = torch.float32 if dtype == "f32" else torch.bfloat16
@@ -46,7 +67,7 @@ def run_masked(torch, op, dtype, values, offsets, mask, scale, select, *, inplac
         mask_guard = torch.full((values.shape[0] + 2, d), 91.0, device="cuda")
         device_mask = mask_guard[1:-1]
         device_mask.copy_(torch.from_numpy(mask))
-    prog = pw_program(op, dtype, d, index, mask is not None, scale, inplace)
+    prog = pw_program(op, dtype, d, index, mask is not None, scale, inplace, fusion)
     report = prog.run(device_values, torch.from_numpy(offsets).to("cuda"), out, mask=device_mask, select=select,
                       mode=mode)
     torch.cuda.synchronize()
@@ -55,8 +76,14 @@ def run_masked(torch, op, dtype, values, offsets, mask, scale, select, *, inplac
         assert torch.all(mask_guard[0] == 91).item() and torch.all(mask_guard[-1] == 91).item()
         np.testing.assert_array_equal(device_mask.cpu().numpy(), mask)
     names = report.kernel_names
-    assert report.pointwise_materialized and names[2 if mode == "checked" else 0] == "pointwise_logits"
-    assert (names[-1] == "pointwise_cast") == (dtype == "bf16")
+    fused = fused_expected(op, dtype, d, report.selected, None if device_mask is None else device_mask.data_ptr(),
+                           inplace_alias=False, fusion=fusion)
+    assert report.pointwise_materialized == (not fused)
+    if fused:
+        assert "pointwise_logits" not in names
+    else:
+        assert names[2 if mode == "checked" else 0] == "pointwise_logits"
+        assert (names[-1] == "pointwise_cast") == (dtype == "bf16")
     return out.float().cpu().numpy().astype(np.float64), report
 
 
@@ -199,3 +226,29 @@ def test_mask_through_the_custom_op(cuda, mode):
     torch.cuda.synchronize()
     check_masked(out.cpu().numpy().astype(np.float64), values.cpu().numpy(), np.array([0, 7, 7, 30]),
                  mask.cpu().numpy(), 1.0, "softmax", "f32")
+
+
+@pytest.mark.parametrize("dtype,d", [("bf16", 128), ("f32", 64), ("bf16", 256)])
+def test_fused_and_materialised_routes_both_match(cuda, dtype, d):
+    """Masked, scaled softmax on the row-balanced and classified schedules,
+    segments of every class (warp, CTA, split normalised in the worker and
+    split left to the normalise kernel): each fused route and the
+    materialised one match the oracle's masked logits."""
+    lengths = np.array([3, 0, 31, 200, 5000, 17, 16000, 1, 90], dtype=np.int64)
+    offsets = offsets_of(lengths)
+    rng = np.random.default_rng(1909)
+    values = prepared(rng.normal(scale=2.0, size=(int(offsets[-1]), d)), dtype)
+    mask = np.where(rng.random(values.shape) < 0.2, -np.inf, rng.uniform(-4, 4, size=values.shape)).astype(np.float32)
+    mask[offsets[1]:offsets[2] + 40, 3] = -np.inf  # a fully masked column inside a segment
+    for select in ("rowbalanced", "classified"):
+        for fusion in (True, False):
+            actual, report = run_masked(cuda, "softmax", dtype, values, offsets, mask, 0.125, select, fusion=fusion)
+            assert report.pointwise_materialized == (not fusion or select == "classified")
+            check_masked(actual, values, offsets, mask, 0.125, "softmax", dtype)
+    # Scale without a mask: the classified worker scales staged rows itself
+    # (a positive scale keeps the packed maximum, a negative one does not).
+    values[7, :4] = [np.inf, -np.inf, np.nan, -np.inf]
+    for scale in (-0.5, 0.5, 3.0):
+        actual, report = run_masked(cuda, "softmax", dtype, values, offsets, None, scale, "classified")
+        assert not report.pointwise_materialized
+        check_masked(actual, values, offsets, None, scale, "softmax", dtype)
