@@ -78,6 +78,8 @@ def parse_args(argv=None):
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-configs", action="store_true", help="skip the c1-c4 entries (N=1)")
     parser.add_argument("--no-parity", action="store_true", help="skip the oracle check of the first call")
+    parser.add_argument("--no-split-fit", action="store_true",
+                        help="keep the model end weight instead of refitting the split from measured rank times")
     parser.add_argument("--cpu-bytes", type=float, default=2e9,
                         help="algorithmic bytes of the CPU sample (one call of each CPU implementation)")
     return parser.parse_args(argv)
@@ -300,11 +302,13 @@ def flush_l2(buffer):
 def time_calls(torch, fn, steps, warmup, stream, flush=None, dist=None):
     """Per-step device time (ms) with CUDA events on ``stream``, the K steps
     bracketed by a barrier and a synchronize on both sides; with ``dist``
-    the per-step times are the maximum over ranks, and the ranks' streams
-    are aligned by a one-element all-reduce right before the first start
-    event (a host barrier returns at different times on different ranks,
-    and the first collective of the step would charge that skew to step 1)."""
-    for _ in range(warmup):
+    the per-step times are the maximum over ranks.  Multi-rank: the ranks'
+    streams are aligned by a one-element all-reduce after the barrier (a
+    host barrier returns at different times on different ranks, and the
+    first collective of a step would charge that skew to step 1), and the
+    last warm-up step runs after it, untimed, so the idle gap of the
+    barrier is not charged to step 1 either."""
+    for _ in range(warmup - (1 if dist is not None and warmup > 0 else 0)):
         if flush is not None:
             flush()
         fn()
@@ -315,6 +319,10 @@ def time_calls(torch, fn, steps, warmup, stream, flush=None, dist=None):
         dist.barrier()
         torch.cuda.synchronize()
         dist.all_reduce(align)
+        if warmup > 0:
+            if flush is not None:
+                flush()
+            fn()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
@@ -436,7 +444,7 @@ def parity_sharded(torch, dist, w, values, out, offsets_host, row0, rank, world,
 def ours(args) -> None:
     import torch
     from ragged import ArtifactCache, Compiler, ProgramSpec
-    from ragged.sharding import END_WEIGHT, balanced_split, segment_owners, shard_rows, torch_exchange
+    from ragged.sharding import (balanced_split, end_weight_model, segment_owners, shard_rows, torch_exchange)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -454,7 +462,9 @@ def ours(args) -> None:
     if world > 1 and w.op == "softmax":
         raise SystemExit("the benchmark's sharded calls compute sum and max; run softmax workloads with --gpus 1")
     offsets_host = w.offsets()
-    splits = balanced_split(offsets_host, world, END_WEIGHT) if world > 1 else None
+    end_weight = end_weight_model(w.op, w.dtype, w.d)
+    split_fit = {"fit": "model weight"}
+    splits = balanced_split(offsets_host, world, end_weight) if world > 1 else None
     rows = shard_rows(w.n, world, rank, splits)
     values = workloads.device_values(w, rows, device)
     offsets = torch.from_numpy(offsets_host).to(device)
@@ -473,6 +483,17 @@ def ours(args) -> None:
     flush = (lambda: flush_l2(flush_buffer)) if flush_buffer is not None else None
     report_holder = {}
     exchange = torch_exchange() if world > 1 else None
+    if world >= 4 and not args.no_split_fit:
+        # Refit the split from measured local phases (the shard kernel and its
+        # fix-up on each rank's rows, exchange left out), then re-shard.
+        end_weight, split_fit, splits = refit_split(torch, dist, program, w, values, offsets, out, offsets_host,
+                                                    world, rank, splits, end_weight)
+        new_rows = shard_rows(w.n, world, rank, splits)
+        if new_rows != rows:
+            del values
+            torch.cuda.empty_cache()
+            rows = new_rows
+            values = workloads.device_values(w, rows, device)
     owners = segment_owners(offsets_host, world, splits) if w.op != "softmax" else None
 
     def step():
@@ -521,7 +542,8 @@ def ours(args) -> None:
             "clocks": clocks.summary()}
     if world > 1:
         line["sharding"] = {"rows_per_rank": [list(shard_rows(w.n, world, r, splits)) for r in range(world)],
-                            "split": f"rows + {END_WEIGHT} x segment ends balanced across ranks",
+                            "split": f"rows + {end_weight:.4g} x segment ends balanced across ranks",
+                            "end_weight_fit": split_fit,
                             "rank_ms": list(RANK_MS),
                             "collective": "NCCL all-gather of edge records",
                             "edge_bytes_per_rank": _native_edge_bytes(w)}
@@ -541,6 +563,37 @@ def ours(args) -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def refit_split(torch, dist, program, w, values, offsets, out, offsets_host, world, rank, splits, weight):
+    """Time each rank's local phase (rg_run_shard + fix-up + combine, with a
+    local stand-in for the exchange, so no rank waits for another) on the
+    current split, fit the end weight to the ranks' times
+    (sharding.fit_end_weight) and return (weight, fit, new split).  Every
+    rank computes the same fit from the all-gathered times."""
+    from ragged.sharding import balanced_split, fit_end_weight, window_ends
+    import statistics as st
+    local = lambda edges: edges.repeat(world)  # same shape as the gathered records
+    times = []
+    for i in range(5):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        program.run_sharded(values, offsets, out, total_rows=w.n, world=world, rank=rank, exchange=local,
+                            splits=splits)
+        end.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            times.append(start.elapsed_time(end))
+    mine = torch.tensor([st.median(times)], dtype=torch.float64, device=values.device)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    rank_ms = [float(t.item()) for t in every]
+    rows = [shard_rows(w.n, world, r, splits)[1] - shard_rows(w.n, world, r, splits)[0] for r in range(world)]
+    ends = window_ends(offsets_host, world, splits)
+    fitted, info = fit_end_weight(rows, ends, rank_ms, weight)
+    info = {**info, "model_weight": round(weight, 4), "fitted_weight": round(fitted, 4),
+            "rank_ms_before": [round(t, 4) for t in rank_ms]}
+    return fitted, info, balanced_split(offsets_host, world, fitted)
 
 
 def side_configs(torch, args, device, stream, cache, peak) -> dict:

@@ -139,8 +139,14 @@ def version() -> str:
     return library().rg_version().decode()
 
 
+_kernel_names: dict[int, str] = {}
+
+
 def kernel_name(kernel_id: int) -> str:
-    return library().rg_kernel_name(kernel_id).decode()
+    name = _kernel_names.get(kernel_id)
+    if name is None:
+        name = _kernel_names[kernel_id] = library().rg_kernel_name(kernel_id).decode()
+    return name
 
 
 _device_info: dict[int, DeviceInfo] = {}

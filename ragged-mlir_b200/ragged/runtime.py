@@ -97,6 +97,11 @@ class CompiledProgram:
         self._workspace: dict[tuple, int] = {}
         tile, vec = spec.optimizations.geometry(spec.feature_dim, spec.dtype)
         self._span = tile * vec
+        self._vector = vec
+        self._dtypes = None  # torch dtypes, resolved on the first call
+        # The report's optimisation section, fixed per program (built once).
+        self._optimization_report = {"requested": spec.optimizations.to_dict(),
+                                     **spec.optimizations.effects(transformed=spec.mask or float(spec.scale) != 1.0)}
         self._flags = (0 if spec.optimizations.vectorize else _native.FLAG_NO_VECTORIZE) | (
             _native.FLAG_IN_PLACE if spec.alias == "inplace" else 0)
         # Scale or mask: rg_run_pointwise (fused into the classified worker's
@@ -133,11 +138,21 @@ class CompiledProgram:
     def close(self) -> None:
         """Nothing to unload: kernels live in the shared library."""
 
+    def _torch_dtypes(self, torch):
+        """(values dtype, offsets dtype) of this specialization, resolved once."""
+        if self._dtypes is None:
+            self._dtypes = ({"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype],
+                            {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype])
+        return self._dtypes
+
     def _validate_tensors(self, values, offsets, out, torch, checked: bool = False, mask=None) -> tuple[int, int]:
-        tensors = (("values", values), ("offsets", offsets), ("out", out)) + ((("mask", mask),) if mask is not None
-                                                                               else ())
-        for name, tensor in tensors:
-            if not isinstance(tensor, torch.Tensor):
+        """The reference's tensor checks and messages (its runtime.py:304-365);
+        each tensor's extent is read once."""
+        tensor_type = torch.Tensor
+        for name, tensor in (("values", values), ("offsets", offsets), ("out", out), ("mask", mask)):
+            if tensor is None and name == "mask":
+                continue
+            if not isinstance(tensor, tensor_type):
                 raise ValidationError(f"{name} must be a torch.Tensor")
             if not tensor.is_cuda:
                 raise RuntimeUnavailable(f"{name} must be on a CUDA device that runs {self.spec.chip} code; "
@@ -146,51 +161,60 @@ class CompiledProgram:
                 raise ValidationError(f"{name} must be row-major contiguous")
             if tensor.requires_grad:
                 raise ValidationError("autograd is outside the supported forward-only contract")
-        if values.device != offsets.device or values.device != out.device:
+        device = values.device
+        if device != offsets.device or device != out.device:
             raise ValidationError("values, offsets and out must use the same CUDA device")
-        if values.ndim != 2 or values.shape[1] != self.spec.feature_dim:
+        shape = values.shape
+        if values.ndim != 2 or shape[1] != self.spec.feature_dim:
             raise ValidationError("values must have shape [N, static D]")
-        if offsets.ndim != 1 or offsets.numel() < 1:
+        count = offsets.numel()
+        if offsets.ndim != 1 or count < 1:
             raise ValidationError("offsets must have shape [B+1], including [0] when B=0")
-        dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[self.spec.dtype]
-        offset_dtype = {"i32": torch.int32, "i64": torch.int64}[self.spec.offsets_dtype]
+        dtype, offset_dtype = self._torch_dtypes(torch)
         if values.dtype != dtype or out.dtype != dtype or offsets.dtype != offset_dtype:
             raise ValidationError("tensor dtype differs from compiled dtype/offsets specialization")
-        _, vector = self.spec.optimizations.geometry(self.spec.feature_dim, self.spec.dtype)
-        if vector > 1:
-            for name, tensor in (("values", values), ("out", out)):
-                if tensor.numel():
-                    need = vector * tensor.element_size()
-                    if tensor.data_ptr() % need:
-                        raise ValidationError(f"{name} must be {need}-byte aligned: this specialization accesses "
-                                              f"{vector} features at a time (compile with vectorize=False for "
-                                              "unaligned views)")
-        n, b = values.shape[0], offsets.numel() - 1
+        n, b = shape[0], count - 1
+        d = shape[1]
+        element = values.element_size()
+        vptr, optr, fptr = values.data_ptr(), out.data_ptr(), offsets.data_ptr()
+        vbytes, obytes, fbytes = n * d * element, out.numel() * element, count * offsets.element_size()
+        if self._vector > 1:
+            need = self._vector * element
+            for name, pointer, size in (("values", vptr, vbytes), ("out", optr, obytes)):
+                if size and pointer % need:
+                    raise ValidationError(f"{name} must be {need}-byte aligned: this specialization accesses "
+                                          f"{self._vector} features at a time (compile with vectorize=False for "
+                                          "unaligned views)")
         if b == 0 and n != 0 and not checked:  # checked mode reports it from the device (final_mismatch)
             raise ValidationError("B=0 requires N=0; values cannot exist without segments")
         if self.spec.offsets_dtype == "i32" and n > 2**31 - 1:
             raise ValidationError("N exceeds the i32 offsets range")
-        expected = (n if self.spec.op == "softmax" else b, self.spec.feature_dim)
+        expected = (n if self.spec.op == "softmax" else b, d)
         if tuple(out.shape) != expected:
             raise ValidationError(f"out shape must be {expected}")
+
+        def overlap(p1, s1, p2, s2):
+            return p1 < p2 + s2 and p2 < p1 + s1
+
         if mask is not None:  # reference runtime.py:346-356; the mask may alias values (read only)
-            if mask.dtype != torch.float32 or tuple(mask.shape) != tuple(values.shape):
+            if mask.dtype != torch.float32 or tuple(mask.shape) != tuple(shape):
                 raise ValidationError("mask must have f32 dtype and exactly values shape [N,D]; "
                                       "broadcasting is unsupported")
-            if mask.device != values.device:
+            if mask.device != device:
                 raise ValidationError("mask must use the values CUDA device")
-            if mask.numel() and mask.data_ptr() % 4:
+            mptr, mbytes = mask.data_ptr(), n * d * 4
+            if mbytes and mptr % 4:
                 raise ValidationError("mask must be 4-byte aligned")
-            if _overlaps(mask, out) or _overlaps(mask, offsets):
+            if overlap(mptr, mbytes, optr, obytes) or overlap(mptr, mbytes, fptr, fbytes):
                 raise ValidationError("mask must not overlap out or offsets")
-        if _overlaps(offsets, values) or _overlaps(offsets, out):
+        if overlap(fptr, fbytes, vptr, vbytes) or overlap(fptr, fbytes, optr, obytes):
             raise ValidationError("offsets must not alias values or out")
         # In place (runtime.py:358-364 of the reference): out must BE values.
-        exact = values.data_ptr() == out.data_ptr() and tuple(values.shape) == tuple(out.shape)
-        if _overlaps(values, out):
+        exact = vptr == optr and tuple(shape) == tuple(out.shape)
+        if overlap(vptr, vbytes, optr, obytes):
             if not exact or self.spec.alias != "inplace":
                 raise ValidationError("out aliases values without a compiler-proven safe in-place schedule")
-        elif self.spec.alias == "inplace" and not (exact and values.numel() == 0):
+        elif self.spec.alias == "inplace" and not (exact and vbytes == 0):
             raise ValidationError("in-place specialization requires out and values to be the same buffer")
         return n, b
 
@@ -452,7 +476,6 @@ class CompiledProgram:
                                (time.perf_counter() - started) * 1000, cache_hit=self.cache_hit,
                                validation_workspace_bytes=checked_bytes,
                                validation_host_ms=validation_ms if validation is not None else None,
-                               optimizations={"requested": self.spec.optimizations.to_dict(),
-                                              **self.spec.optimizations.effects(transformed=self._pointwise)},
+                               optimizations=dict(self._optimization_report),
                                pointwise_materialized=self._pointwise and "pointwise_logits" in names,
                                d_tile=tile, d_vector=vec, streams=streams, selected=schedule, selection=selection)

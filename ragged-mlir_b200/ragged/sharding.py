@@ -35,6 +35,52 @@ from .errors import ValidationError
 END_WEIGHT = 1.25
 
 
+def end_weight_model(op: str, dtype: str, d: int) -> float:
+    """Starting weight of a segment end, in rows: an end writes one output
+    row and restarts the accumulators, about 128 bytes of streaming on B200
+    beyond the row (the round-1 hand fit for bf16 D=256: 1.25 rows), so
+    1 + 128 / row bytes.  Refined from measured rank times by
+    ``fit_end_weight``."""
+    row_bytes = d * (2 if dtype == "bf16" else 4)
+    return 1.0 + 128.0 / row_bytes if op != "softmax" else 128.0 / row_bytes
+
+
+def window_ends(offsets: np.ndarray, world: int, splits) -> list[int]:
+    """Segment ends each rank's window consumes (ends in (row0, row1], and
+    on rank 0 also the ends at row 0)."""
+    offsets = np.asarray(offsets, dtype=np.int64)
+    n = int(offsets[-1])
+    ends = offsets[1:]
+    counts = []
+    for rank in range(world):
+        row0, row1 = shard_rows(n, world, rank, splits)
+        lo = 0 if rank == 0 else int(np.searchsorted(ends, row0, side="right"))
+        counts.append(int(np.searchsorted(ends, row1, side="right")) - lo)
+    return counts
+
+
+def fit_end_weight(rows, ends, times_ms, fallback: float) -> tuple[float, dict]:
+    """End weight from measured per-rank times of the local phase: the
+    least-squares fit t = c + a * rows + e * ends over the ranks (a, e >= 0),
+    weight e / a.  Needs at least four ranks with different mixes of rows
+    and ends; otherwise ``fallback`` is returned."""
+    rows = np.asarray(rows, dtype=np.float64)
+    ends = np.asarray(ends, dtype=np.float64)
+    times = np.asarray(times_ms, dtype=np.float64)
+    info = {"ranks": len(times)}
+    if len(times) < 4 or np.ptp(ends) == 0 or np.ptp(rows) == 0:
+        return fallback, {**info, "fit": "not enough distinct ranks; model weight kept"}
+    from scipy.optimize import nnls
+    a = np.stack([np.ones_like(rows), rows / 1e6, ends / 1e6], axis=1)
+    coef, residual = nnls(a, times)
+    if coef[1] <= 0:
+        return fallback, {**info, "fit": "no per-row cost in the fit; model weight kept"}
+    weight = float(np.clip(coef[2] / coef[1], 0.0, 64.0))
+    return weight, {**info, "fit": "least squares over ranks", "ms_fixed": round(float(coef[0]), 4),
+                    "ms_per_mrow": round(float(coef[1]), 5), "ms_per_mend": round(float(coef[2]), 5),
+                    "residual_ms": round(float(residual), 5)}
+
+
 def shard_rows(n: int, world: int, rank: int, splits=None) -> tuple[int, int]:
     """Rows [row0, row1) of ``rank``: from ``splits`` (world + 1 row
     boundaries, e.g. ``balanced_split``) or the even row split (the split

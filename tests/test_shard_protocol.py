@@ -366,3 +366,24 @@ def test_native_split_arguments_must_hold_world_plus_one_boundaries(splits):
         _native.shard_segments(offsets, "i64", 3, 1, splits)
     with pytest.raises(ValidationError, match="world \\+ 1"):
         _native.shard_workspace_bytes("sum", "f32", "i64", 4, 540, 3, 3, 1, 0, splits)
+
+
+def test_end_weight_fit_recovers_the_cost_of_an_end():
+    """sharding.fit_end_weight: per-rank times made from a known fixed cost,
+    per-row cost and per-end cost give back their ratio; too few ranks keep
+    the model weight.  window_ends counts each end on exactly one rank."""
+    from ragged.sharding import balanced_split, end_weight_model, fit_end_weight, window_ends
+    rng = np.random.default_rng(12)
+    rows = rng.integers(5_000_000, 30_000_000, size=8)
+    ends = rng.integers(0, 2_000_000, size=8)
+    times = 0.04 + rows * 9e-8 + ends * 2.7e-7
+    weight, info = fit_end_weight(rows, ends, times, fallback=1.25)
+    assert weight == pytest.approx(3.0, rel=1e-6) and info["fit"] == "least squares over ranks"
+    assert fit_end_weight(rows[:2], ends[:2], times[:2], fallback=1.25)[0] == 1.25
+    assert end_weight_model("sum", "bf16", 256) == 1.25
+    lengths = make_lengths("long_tail", 500, 100_000, seed=2)
+    lengths[:40] = 0
+    offsets = offsets_of(lengths)
+    for world in (1, 3, 8):
+        for splits in (None, balanced_split(offsets, world, 4.0)):
+            assert sum(window_ends(offsets, world, splits)) == offsets.size - 1
