@@ -79,6 +79,17 @@ int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
 int launch_rowbal(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
 // Resident CTAs per SM of a row-balanced kernel, cached per (kernel, device).
 int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks);
+// Virtual CTAs a row-balanced launch wants for `path` merge-path items:
+// 64 items per unit, fewer (down to 8) when that leaves the `resident`
+// CTAs idle, so a small call spreads over the GPU instead of a few CTAs
+// whose threads each walk 64 items (and one thread each merges their pieces).
+inline int64_t rowbal_wanted_ctas(int64_t path, int64_t resident, int units_per_cta) {
+  int64_t per_unit = path / (resident * units_per_cta);
+  per_unit = per_unit < 8 ? 8 : (per_unit > 64 ? 64 : per_unit);
+  const int64_t chunk = per_unit * units_per_cta;
+  const int64_t wanted = (path + chunk - 1) / chunk;
+  return wanted < 1 ? 1 : wanted;
+}
 int classified_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
 // Softmax on the classified schedule with the input transform (scale,
 // additive mask) fused into the loads: for rows the pipelined worker stages.

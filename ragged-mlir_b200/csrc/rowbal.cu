@@ -79,7 +79,7 @@ struct Plan {
   int64_t stats, stats_bytes;                  // softmax statistics
 };
 
-// No more than one unit per 64 path items; the packed kernel runs one
+// Units of 8 to 64 path items (rowbal_wanted_ctas); the packed kernel runs one
 // resident wave, the row-balanced kernel kVirtualPerCta virtual CTAs per
 // resident CTA.
 int make_plan(const Problem &p, const Geometry &g, const void *kernel, const void *packed, Plan *plan) {
@@ -91,11 +91,11 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
   if (status) return status;
   const int units_per_cta = (kRowbalThreads / 32) << (5 - g.g_shift);
   const int64_t path = p.n + p.b;
-  const int64_t wanted = (path + 64 * units_per_cta - 1) / (64 * units_per_cta);
   int64_t resident = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
   if (resident < 1) resident = 1;
+  const int64_t wanted = rowbal_wanted_ctas(path, resident, units_per_cta);
   int64_t vctas = resident * virtual_per_cta(path, resident);
-  if (vctas > wanted) vctas = wanted < 1 ? 1 : wanted;
+  if (vctas > wanted) vctas = wanted;
   plan->vctas = vctas;
   plan->grid = resident < vctas ? resident : vctas;
   plan->packed_ctas = 0;
@@ -103,8 +103,8 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
     int packed_per_sm = 0;
     status = rowbal_occupancy(packed, dev.device, kRowbalThreads, &packed_per_sm);
     if (status) return status;
-    const int64_t packed_wanted = (path + 64 * kRowbalThreads - 1) / (64 * kRowbalThreads);
     int64_t ctas = static_cast<int64_t>(packed_per_sm) * dev.sm_count;
+    const int64_t packed_wanted = rowbal_wanted_ctas(path, ctas, kRowbalThreads);
     if (ctas > packed_wanted) ctas = packed_wanted;
     plan->packed_ctas = ctas < 1 ? 1 : ctas;
   }

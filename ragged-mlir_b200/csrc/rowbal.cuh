@@ -547,16 +547,59 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   // a segment whose TAIL, THROUGH and HEAD pieces all lie in this CTA is
   // finished here; what remains is at most one CTA-level HEAD (a segment
   // open at the CTA's start that ends in it) and one TAIL / THROUGH (open
-  // at its end), written to global memory for the fix-up.
-  if (threadIdx.x < G) {
-    const int c_lane = threadIdx.x;
-    const int c_cv = tile * 32 + c_lane;
-    float *const cta_pieces = pieces + vcta * 2 * W * d;
-    const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
-    auto piece = [&](int k, int slot) { return &s_piece[slot][((k << g_shift) + c_lane) * VEC * W]; };
-    combine_pieces<T, OP, VEC>(units_per_cta, piece, VEC, s_head, s_tail, s_kind, c_cv < vec_cols, out, d, c_col,
-                               cta_pieces + c_col, cta_pieces + W * d + c_col, d,
-                               tile == 0 && c_lane == 0 ? &meta[vcta] : nullptr, window.seg0, window.seg1);
+  // at its end), written to global memory for the fix-up.  With several
+  // units per warp (rows narrower than 32 vectors) the merge is two-level:
+  // each warp merges its own units (their pieces are its lanes' registers
+  // stored in shared memory, so a __syncwarp orders them), leaving its
+  // HEAD and TAIL / THROUGH in its first unit's slots, then the warps'
+  // pieces merge across the CTA -- 32 / G + 8 dependent merges per column
+  // instead of 256 / G.
+  constexpr int NW = kRowbalThreads / 32;
+  __shared__ int64_t w_head[NW], w_tail[NW];
+  __shared__ int32_t w_kind[NW];
+  const int upw = 32 >> g_shift;  // units per warp
+  const int c_cv_base = tile * 32;
+  if (upw == 1) {
+    if (threadIdx.x < G) {
+      const int c_lane = threadIdx.x;
+      const int c_cv = c_cv_base + c_lane;
+      float *const cta_pieces = pieces + vcta * 2 * W * d;
+      const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
+      auto piece = [&](int k, int slot) { return &s_piece[slot][((k << g_shift) + c_lane) * VEC * W]; };
+      combine_pieces<T, OP, VEC>(units_per_cta, piece, VEC, s_head, s_tail, s_kind, c_cv < vec_cols, out, d, c_col,
+                                 cta_pieces + c_col, cta_pieces + W * d + c_col, d,
+                                 tile == 0 && c_lane == 0 ? &meta[vcta] : nullptr, window.seg0, window.seg1);
+    }
+  } else {
+    const int warp = threadIdx.x >> 5;
+    if (q == 0) {  // level 1: lanes gl of the warp's first unit
+      const int c_cv = c_cv_base + gl;
+      const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
+      const int first_unit = warp * upw;
+      auto piece = [&](int k, int slot) {
+        return &s_piece[slot][(((first_unit + k) << g_shift) + gl) * VEC * W];
+      };
+      UnitMeta m;
+      combine_pieces<T, OP, VEC>(upw, piece, VEC, s_head + first_unit, s_tail + first_unit, s_kind + first_unit,
+                                 c_cv < vec_cols, out, d, c_col, piece(0, 0), piece(0, 1), VEC,
+                                 gl == 0 ? &m : nullptr, window.seg0, window.seg1);
+      if (gl == 0) {
+        w_head[warp] = m.head_seg;
+        w_tail[warp] = m.tail_seg;
+        w_kind[warp] = m.tail_kind;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {  // level 2: the warps' pieces, in warp order
+      const int c_lane = threadIdx.x;
+      const int c_cv = c_cv_base + c_lane;
+      float *const cta_pieces = pieces + vcta * 2 * W * d;
+      const int64_t c_col = static_cast<int64_t>(c_cv) * VEC;
+      auto piece = [&](int k, int slot) { return &s_piece[slot][(((k * upw) << g_shift) + c_lane) * VEC * W]; };
+      combine_pieces<T, OP, VEC>(NW, piece, VEC, w_head, w_tail, w_kind, c_cv < vec_cols, out, d, c_col,
+                                 cta_pieces + c_col, cta_pieces + W * d + c_col, d,
+                                 tile == 0 && c_lane == 0 ? &meta[vcta] : nullptr, window.seg0, window.seg1);
+    }
   }
     if (!work) break;
     __syncthreads();  // the combine is done with the shared pieces before the next virtual CTA

@@ -67,7 +67,7 @@ constexpr int64_t kAlign = 256;
 int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 // Virtual CTAs of the row-balanced kernel (several per resident CTA, taken
-// from a counter), no more than one unit per 64 items of the window's path
+// from a counter), units of 8 to 64 items of the window's path
 // (bounded by its rows plus all segment ends).
 template <typename T, typename OffT, int OP, int VEC>
 int shard_plan(const Problem &p, const Geometry &g, int64_t rows, int64_t slots, ShardPlan *plan) {
@@ -81,11 +81,10 @@ int shard_plan(const Problem &p, const Geometry &g, int64_t rows, int64_t slots,
   int64_t resident = static_cast<int64_t>(per_sm) * dev.sm_count / g.col_tiles;
   if (resident < 1) resident = 1;
   const int64_t path = rows + p.b;
-  const int64_t wanted = (path + 64 * units_per_cta - 1) / (64 * units_per_cta);
+  const int64_t wanted = rowbal_wanted_ctas(path, resident, units_per_cta);
   const int64_t per = path / (resident * 16384);  // as the single-GPU plan: up to 8 per CTA
   int64_t vctas = resident * (per < 1 ? 1 : (per > 8 ? 8 : per));
   if (vctas > wanted) vctas = wanted;
-  if (vctas < 1) vctas = 1;
   plan->vctas = vctas;
   plan->grid = resident < vctas ? resident : vctas;
   const int width = OP == OP_MAX ? 1 : 2;
