@@ -77,8 +77,9 @@ int check_device(DeviceProps *props);     // current device must be sm_100
 int launch_naive(const Problem &p, const Geometry &g, cudaStream_t stream, rg_report *report);
 int rowbal_workspace(const Problem &p, const Geometry &g, int64_t *bytes);
 int launch_rowbal(const Problem &p, const Geometry &g, void *workspace, cudaStream_t stream, rg_report *report);
-// Resident CTAs per SM of a row-balanced kernel, cached per (kernel, device).
-int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks);
+// Resident CTAs per SM of a row-balanced kernel launched with `smem` bytes
+// of dynamic shared memory, cached per (kernel, device).
+int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks, int smem = 0);
 // Virtual CTAs a row-balanced launch wants for `path` merge-path items:
 // 64 items per unit, fewer (down to 8) when that leaves the `resident`
 // CTAs idle, so a small call spreads over the GPU instead of a few CTAs

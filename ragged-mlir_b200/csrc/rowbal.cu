@@ -13,9 +13,9 @@ std::mutex g_occupancy_mutex;
 std::map<std::pair<const void *, int>, int> g_occupancy;  // (kernel, device) -> blocks per SM
 }  // namespace
 
-// Resident CTAs per SM of a row-balanced kernel (kRowbalSmem dynamic shared
-// memory), queried once per (kernel, device) and cached.
-int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks) {
+// Resident CTAs per SM of a row-balanced kernel (`smem` bytes of dynamic
+// shared memory), queried once per (kernel, device) and cached.
+int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks, int smem) {
   const auto key = std::make_pair(kernel, device);
   std::lock_guard<std::mutex> lock(g_occupancy_mutex);
   auto it = g_occupancy.find(key);
@@ -24,7 +24,7 @@ int rowbal_occupancy(const void *kernel, int device, int threads, int *blocks) {
     return RG_OK;
   }
   int n = 0;
-  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, kRowbalSmem),
+  int status = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem),
                       "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   if (status) return status;
   g_occupancy[key] = n < 1 ? 1 : n;
@@ -51,10 +51,16 @@ bool packs(const Problem &p, const Geometry &g) {
   return !(p.flags & RG_FLAG_NO_VECTORIZE) && row_bytes < 16 && 16 % row_bytes == 0 && g.vec == p.d;
 }
 
+// The packed kernel, its staging area (above the 48 KB default of dynamic
+// shared memory) allowed on the current device; null where it does not apply.
 template <typename T, typename OffT, int OP, int VEC>
-const void *packed_ptr() {
+const void *packed_ptr(int *status) {
+  *status = RG_OK;
   if constexpr (VEC * sizeof(T) < 16 && OP != OP_SOFTMAX) {
-    return reinterpret_cast<const void *>(&rowbal_packed_kernel<T, OffT, OP, VEC>);
+    const void *kernel = reinterpret_cast<const void *>(&rowbal_packed_kernel<T, OffT, OP, VEC>);
+    *status = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackedStageBytes),
+                         "cudaFuncSetAttribute(rowbal_packed_kernel)");
+    return kernel;
   }
   return nullptr;
 }
@@ -101,7 +107,7 @@ int make_plan(const Problem &p, const Geometry &g, const void *kernel, const voi
   plan->packed_ctas = 0;
   if (packed) {
     int packed_per_sm = 0;
-    status = rowbal_occupancy(packed, dev.device, kRowbalThreads, &packed_per_sm);
+    status = rowbal_occupancy(packed, dev.device, kRowbalThreads, &packed_per_sm, kPackedStageBytes);
     if (status) return status;
     int64_t ctas = static_cast<int64_t>(packed_per_sm) * dev.sm_count;
     const int64_t packed_wanted = rowbal_wanted_ctas(path, ctas, kRowbalThreads);
@@ -127,8 +133,10 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
               rg_report *report, const Xform &xf = Xform{}) {
   static_assert(!XF || OP == OP_SOFTMAX, "the fused transform is a softmax route");
   Plan plan;
-  const void *packed = XF ? nullptr : (packs(p, g) ? packed_ptr<T, OffT, OP, VEC>() : nullptr);
-  int status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC, XF>(), packed, &plan);
+  int status = RG_OK;
+  const void *packed = XF ? nullptr : (packs(p, g) ? packed_ptr<T, OffT, OP, VEC>(&status) : nullptr);
+  if (status) return status;
+  status = make_plan(p, g, kernel_ptr<T, OffT, OP, VEC, XF>(), packed, &plan);
   if (status) return status;
   if (bytes) {
     *bytes = plan.stats + plan.stats_bytes;
@@ -140,10 +148,10 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
     if (packed && reinterpret_cast<uintptr_t>(p.values) % 16 == 0) {
       const int64_t ctas = plan.packed_ctas;
       dim3 grid(static_cast<unsigned>(ctas), 1, 1);
-      rowbal_packed_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, 0, stream>>>(
+      rowbal_packed_kernel<T, OffT, OP, VEC><<<grid, kRowbalThreads, kPackedStageBytes, stream>>>(
           static_cast<const T *>(p.values), static_cast<const OffT *>(p.offsets), static_cast<T *>(p.out), p.n, p.b,
           ctas * kRowbalThreads, pieces, meta);
-      record_launch(report, K_ROWBAL_PACKED, grid, kRowbalThreads, 0);
+      record_launch(report, K_ROWBAL_PACKED, grid, kRowbalThreads, kPackedStageBytes);
       status = check_cuda(cudaGetLastError(), "rowbal_packed_kernel launch");
       if (status || ctas < 2) return status;
       dim3 fix_grid(static_cast<unsigned>(ctas), 1, 1);

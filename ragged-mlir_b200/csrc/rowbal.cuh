@@ -83,6 +83,17 @@ struct RowAcc<OP_SUM, VEC> {
     for (int v = 0; v < VEC; ++v) { kahan_add(s[v], c[v], p[v]); p[v] = 0.0f; }
     count = 0;
   }
+  // Runs of rows: fold_raw adds a row to the plain block without counting
+  // it; account(rows) counts the run and closes the block once it holds
+  // kSumBlock rows or more.
+  __device__ __forceinline__ void fold_raw(const float (&x)[VEC]) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) p[v] = __fadd_rn(p[v], x[v]);
+  }
+  __device__ __forceinline__ void account(int rows) {
+    count += rows;
+    if (count >= kSumBlock) settle();
+  }
   __device__ __forceinline__ void value(float (&y)[VEC]) {
     settle();
 #pragma unroll
@@ -117,6 +128,8 @@ struct RowAcc<OP_MAX, VEC> {
 #pragma unroll
     for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], x[v]);
   }
+  __device__ __forceinline__ void fold_raw(const float (&x)[VEC]) { fold(x); }
+  __device__ __forceinline__ void account(int) {}
   __device__ __forceinline__ void value(float (&y)[VEC]) {
 #pragma unroll
     for (int v = 0; v < VEC; ++v) y[v] = m[v];
@@ -607,15 +620,30 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
 }
 
 // Narrow rows (D * sizeof(T) in {2, 4, 8} bytes): every lane is a unit and
-// reads 16-byte packets of R = 16 / (D * sizeof(T)) whole rows, folding a
-// packet at once when no segment boundary falls inside it.  A warp finds
-// its slice of the merge path with a 32-ary search; each lane then finds
-// its own slice by binary search inside the warp's segment range.  The next
-// four segment ends sit in a register window that is refilled one entry
-// per finished segment, so short segments do not wait on offsets loads.
+// folds 16-byte packets of R = 16 / (D * sizeof(T)) whole rows, a packet at
+// once when no segment boundary falls inside it.  A warp finds its slice of
+// the merge path with a 32-ary search; each lane then finds its own slice by
+// binary search inside the warp's segment range.  The next four segment
+// ends sit in a register window that is refilled one entry per finished
+// segment, so short segments do not wait on offsets loads.
+//
+// A lane's rows are contiguous but far from its neighbours', so a warp load
+// of one packet per lane would touch 32 lines.  Instead the warp stages its
+// lanes' next kPackedRun packets (128 bytes each) into shared memory with
+// cp.async, each instruction copying the runs of 32 / kPackedRun lanes
+// (whole 128-byte runs, 4 lines per instruction), two rounds in flight
+// while the lanes fold the previous one from shared memory.  A lane's run
+// occupies kPackedRun + 1 slots, so the eight lanes of a 16-byte shared
+// load phase read eight different bank groups.
+//
 // Pieces are combined per warp (lane 0 over 32 units) and then per CTA
 // (thread 0 over the 8 warps), leaving one HEAD and one TAIL / THROUGH per
 // CTA for the fix-up kernel.
+constexpr int kPackedRun = 8;     // packets per lane per staged round
+constexpr int kPackedStages = 2;  // rounds in flight per warp
+constexpr int kPackedStageBytes =
+    (kRowbalThreads / 32) * kPackedStages * 32 * (kPackedRun + 1) * 16;  // dynamic shared memory per CTA
+static_assert(32 % kPackedRun == 0, "a staging instruction copies whole runs of 32 / kPackedRun lanes");
 
 // First k in [lo, hi] with offsets[k+1] + k >= diag, for one thread.
 template <typename OffT>
@@ -627,7 +655,7 @@ __device__ __forceinline__ int64_t path_search_range(const OffT *offsets, int64_
   return lo;
 }
 
-template <typename T, typename OffT, int OP, int DS, int U = 4, int MINB = 3>
+template <typename T, typename OffT, int OP, int DS, int U = 4, int MINB = 2>
 __global__ void __launch_bounds__(kRowbalThreads, MINB)
 rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T *__restrict__ out,
                      int64_t n, int64_t b, int64_t units, float *__restrict__ pieces, UnitMeta *__restrict__ meta) {
@@ -684,42 +712,96 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
     w2 = w3;
     w3 = end_at(seg + 4);
   };
-  auto fold_row = [&](const float (&x)[E], int k) {
+  // Staged rows are read from shared memory; rows outside this lane's
+  // slice read as the operation's identity (0 for sum, -inf for max).
+  auto fold_row_if = [&](const float (&x)[E], int k, bool in) {
     float row[DS];
 #pragma unroll
-    for (int f = 0; f < DS; ++f) row[f] = x[k * DS + f];
-    acc.fold(row);
+    for (int f = 0; f < DS; ++f) row[f] = in ? x[k * DS + f] : (OP == OP_MAX ? -kInf : 0.0f);
+    acc.fold_raw(row);
   };
 
   const uint4 *packets = reinterpret_cast<const uint4 *>(values);
   const int64_t p_begin = j0 / R, p_end = (j1 + R - 1) / R;
-  for (int64_t p = p_begin; p < p_end; p += U) {
-    uint4 raw[U];
+  const int my_packets = static_cast<int>(p_end - p_begin);
+  __shared__ int64_t s_pbegin[kRowbalThreads];
+  __shared__ int32_t s_pcount[kRowbalThreads];
+  s_pbegin[threadIdx.x] = p_begin;
+  s_pcount[threadIdx.x] = my_packets;
+  const int rounds = (__reduce_max_sync(0xffffffffu, my_packets) + kPackedRun - 1) / kPackedRun;
+  __syncwarp();
+  extern __shared__ uint4 s_stage[];  // [NW][kPackedStages][32][kPackedRun + 1]
+  constexpr int kLaneSlots = kPackedRun + 1, kStageSlots = 32 * kLaneSlots;
+  constexpr int kRunsPerCopy = 32 / kPackedRun;
+  uint4 *const w_stage = s_stage + warp * kPackedStages * kStageSlots;
+  // This lane's copies: copy m moves packet k_copy of the run of lane
+  // m * kRunsPerCopy + lane / kPackedRun, in every round.
+  const int k_copy = lane % kPackedRun;
+  const uint4 *copy_src[kPackedRun];
+  int copy_left[kPackedRun];  // round r copies while r * kPackedRun < copy_left
 #pragma unroll
-    for (int t = 0; t < U; ++t)
-      if (p + t < p_end) raw[t] = __ldg(packets + p + t);
+  for (int m = 0; m < kPackedRun; ++m) {
+    const int src = warp * 32 + m * kRunsPerCopy + lane / kPackedRun;
+    copy_src[m] = packets + s_pbegin[src] + k_copy;
+    copy_left[m] = s_pcount[src] - k_copy;
+  }
+  const uint32_t copy_dst = smem_u32(w_stage) + ((lane / kPackedRun) * kLaneSlots + k_copy) * 16;
+  auto issue = [&](int r) {
+    const uint32_t dst = copy_dst + (r % kPackedStages) * kStageSlots * 16;
+    const int idx = r * kPackedRun;
 #pragma unroll
-    for (int t = 0; t < U; ++t) {
-      if (p + t < p_end) {
-        float x[E];
-        VecIO<T, E>::unpack(*reinterpret_cast<const typename VecIO<T, E>::Raw *>(&raw[t]), x);
-        const int64_t r0 = (p + t) * R;
-        if (r0 >= j0 && r0 + R <= j1 && w0 >= r0 + R) {
+    for (int m = 0; m < kPackedRun; ++m)
+      if (idx < copy_left[m]) cp_async<16>(dst + m * kRunsPerCopy * kLaneSlots * 16, copy_src[m] + idx);
+    cp_async_commit();
+  };
 #pragma unroll
-          for (int k = 0; k < R; ++k) fold_row(x, k);
+  for (int r = 0; r < kPackedStages; ++r) issue(r);
+  constexpr int kRunRows = kPackedRun * R;
+  for (int r = 0; r < rounds; ++r) {
+    cp_async_wait<kPackedStages - 1>();
+    __syncwarp();
+    const uint4 *const mine = w_stage + (r % kPackedStages) * kStageSlots + lane * kLaneSlots;
+    const int64_t run_row = (p_begin + static_cast<int64_t>(r) * kPackedRun) * R;  // first staged row
+    const int64_t lo = j0 > run_row ? j0 : run_row;
+    const int64_t hi = j1 < run_row + kRunRows ? j1 : run_row + kRunRows;
+    if (lo < hi) {
+      while (w0 <= lo) finish();
+      const int a = static_cast<int>(lo - run_row), e = static_cast<int>(hi - run_row);
+      if (w0 >= hi) {
+        // No segment ends inside [lo, hi): fold the staged rows at once.
+        if (a == 0 && e == kRunRows) {
+#pragma unroll
+          for (int k = 0; k < kPackedRun; ++k) {
+            float x[E];
+            VecIO<T, E>::unpack(*reinterpret_cast<const typename VecIO<T, E>::Raw *>(&mine[k]), x);
+#pragma unroll
+            for (int kk = 0; kk < R; ++kk) fold_row_if(x, kk, true);
+          }
         } else {
 #pragma unroll
-          for (int k = 0; k < R; ++k) {
-            const int64_t r = r0 + k;
-            if (r >= j0 && r < j1) {
-              while (w0 <= r) finish();
-              fold_row(x, k);
-            }
+          for (int k = 0; k < kPackedRun; ++k) {
+            float x[E];
+            VecIO<T, E>::unpack(*reinterpret_cast<const typename VecIO<T, E>::Raw *>(&mine[k]), x);
+#pragma unroll
+            for (int kk = 0; kk < R; ++kk) fold_row_if(x, kk, k * R + kk >= a && k * R + kk < e);
           }
+        }
+        acc.account(e - a);
+      } else {
+        // A segment ends inside: row by row.
+        const T *const rows = reinterpret_cast<const T *>(mine);
+        for (int i = a; i < e; ++i) {
+          while (w0 <= run_row + i) finish();
+          float x[DS];
+          VecIO<T, DS>::unpack(*reinterpret_cast<const typename VecIO<T, DS>::Raw *>(rows + i * DS), x);
+          acc.fold(x);
         }
       }
     }
+    __syncwarp();  // every lane is done with this stage before it is refilled
+    issue(r + kPackedStages);
   }
+  cp_async_wait<0>();  // the groups issued past the last round are empty
   while (seg < i1) finish();
   if (seg < b) {
     const int64_t start = load_offset(offsets, seg);
