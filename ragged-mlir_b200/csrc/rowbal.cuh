@@ -114,6 +114,23 @@ struct RowAcc<OP_SUM, VEC> {
 #pragma unroll
     for (int v = 0; v < VEC; ++v) kahan_merge(s[v], c[v], piece[v], piece[stride + v]);
   }
+  // Warp scans over settled accumulators: the value of lane - delta, and
+  // this = this (earlier rows) + later.
+  __device__ __forceinline__ RowAcc shfl_up(int delta) const {
+    RowAcc r;
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      r.s[v] = __shfl_up_sync(0xffffffffu, s[v], delta);
+      r.c[v] = __shfl_up_sync(0xffffffffu, c[v], delta);
+      r.p[v] = 0.0f;
+    }
+    r.count = 0;
+    return r;
+  }
+  __device__ __forceinline__ void merge(const RowAcc &later) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) kahan_merge(s[v], c[v], later.s[v], later.c[v]);
+  }
 };
 
 template <int VEC>
@@ -145,6 +162,16 @@ struct RowAcc<OP_MAX, VEC> {
   __device__ __forceinline__ void merge_piece(const float *piece, int64_t) {
 #pragma unroll
     for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], piece[v]);
+  }
+  __device__ __forceinline__ RowAcc shfl_up(int delta) const {
+    RowAcc r;
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) r.m[v] = __shfl_up_sync(0xffffffffu, m[v], delta);
+    return r;
+  }
+  __device__ __forceinline__ void merge(const RowAcc &later) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) m[v] = max_nan(m[v], later.m[v]);
   }
 };
 
@@ -767,9 +794,10 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
     if (lo < hi) {
       while (w0 <= lo) finish();
       const int a = static_cast<int>(lo - run_row), e = static_cast<int>(hi - run_row);
-      if (w0 >= hi) {
-        // No segment ends inside [lo, hi): fold the staged rows at once.
-        if (a == 0 && e == kRunRows) {
+      // Fold staged rows [from, to) in one pass (predicated unless the pass
+      // covers the whole run).
+      auto pass = [&](int from, int to) {
+        if (from == 0 && to == kRunRows) {
 #pragma unroll
           for (int k = 0; k < kPackedRun; ++k) {
             float x[E];
@@ -783,12 +811,24 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
             float x[E];
             VecIO<T, E>::unpack(*reinterpret_cast<const typename VecIO<T, E>::Raw *>(&mine[k]), x);
 #pragma unroll
-            for (int kk = 0; kk < R; ++kk) fold_row_if(x, kk, k * R + kk >= a && k * R + kk < e);
+            for (int kk = 0; kk < R; ++kk) fold_row_if(x, kk, k * R + kk >= from && k * R + kk < to);
           }
         }
-        acc.account(e - a);
+        acc.account(to - from);
+      };
+      if (w2 >= hi) {
+        // At most two segment ends inside [lo, hi): one pass per piece
+        // between them (a run of empty segments ending at the same row is
+        // finished between two passes).
+        for (int cur = a;;) {
+          const int stop = w0 < hi ? static_cast<int>(w0 - run_row) : e;
+          pass(cur, stop);
+          if (stop == e) break;
+          do finish(); while (w0 <= run_row + stop);
+          cur = stop;
+        }
       } else {
-        // A segment ends inside: row by row.
+        // Three or more ends inside: row by row.
         const T *const rows = reinterpret_cast<const T *>(mine);
         for (int i = a; i < e; ++i) {
           while (w0 <= run_row + i) finish();
@@ -812,16 +852,55 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
     }
   }
   __syncwarp();
-  // Level 1: lane 0 of each warp combines its 32 units.
-  if (lane == 0) {
-    const int base = warp * 32;
-    auto piece = [&](int k, int slot) { return &s_piece[slot][(base + k) * DS * W]; };
-    UnitMeta m;
-    combine_pieces<T, OP, DS>(32, piece, DS, s_head + base, s_tail + base, s_kind + base, true, out, DS, 0,
-                              &w_piece[0][warp * DS * W], &w_piece[1][warp * DS * W], DS, &m, 0, 0);
-    w_head[warp] = m.head_seg;
-    w_tail[warp] = m.tail_seg;
-    w_kind[warp] = m.tail_kind;
+  // Level 1: the warp's 32 units by a segmented scan of their TAIL /
+  // THROUGH pieces across lanes (a TAIL -- a segment starting in the lane --
+  // restarts the scan; a lane without a piece passes it on).  A lane with a
+  // HEAD adds the scan of the lanes before it: the segment is finished if a
+  // TAIL precedes it in the warp (its start), else the sum is the warp's
+  // HEAD piece.  The last lane with path items holds the warp's open piece.
+  {
+    const unsigned full = 0xffffffffu;
+    const int kind = s_kind[threadIdx.x];
+    Acc run;
+    if (kind != PIECE_NONE) run.load_piece(my_tail, DS); else run.init();
+    bool restart = kind == PIECE_TAIL;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      Acc up = run.shfl_up(off);
+      const bool up_restart = __shfl_up_sync(full, restart, off);
+      if (lane >= off && !restart) {
+        up.merge(run);
+        run = up;
+        restart = up_restart;
+      }
+    }
+    Acc before = run.shfl_up(1);  // the scan up to the previous lane
+    const bool before_tail = __shfl_up_sync(full, restart, 1) && lane > 0;
+    const int64_t h = s_head[threadIdx.x];
+    const bool warp_head = h >= 0 && !before_tail;
+    if (h >= 0) {
+      if (lane == 0) before.init();
+      Acc head;
+      head.load_piece(my_head, DS);
+      before.merge(head);
+      if (before_tail) {
+        float y[DS];
+        before.value(y);
+        VecIO<T, DS>::store(out + h * DS, y);
+      } else {
+        before.store_piece(&w_piece[0][warp * DS * W], DS);
+      }
+    }
+    const unsigned head_lanes = __ballot_sync(full, warp_head);  // at most one lane
+    if (lane == (head_lanes ? __ffs(head_lanes) - 1 : 0)) w_head[warp] = warp_head ? h : -1;
+    const unsigned busy = __ballot_sync(full, d1 > d0);
+    const int last = busy ? 31 - __clz(busy) : 0;
+    if (lane == last) {
+      const bool open = busy && kind != PIECE_NONE;
+      if (open) run.store_piece(&w_piece[1][warp * DS * W], DS);
+      w_tail[warp] = open ? s_tail[threadIdx.x] : -1;
+      w_kind[warp] = open ? (restart ? PIECE_TAIL : PIECE_THROUGH) : PIECE_NONE;
+    }
   }
   __syncthreads();
   // Level 2: thread 0 combines the warps into the CTA's pieces.

@@ -248,6 +248,33 @@ def test_narrow_rows_packed_and_unaligned(cuda, op, dtype, d):
             assert "rowbalanced" in names and "rowbalanced_packed" not in names
 
 
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("dtype,d", [("f32", 1), ("f32", 2), ("bf16", 1), ("bf16", 4)])
+@pytest.mark.parametrize("index", ["i32", "i64"])
+def test_packed_segment_ends_inside_staged_runs(cuda, op, dtype, d, index):
+    """The packed kernel folds a staged run of 8 packets in one pass per
+    piece between segment ends (up to two ends), row by row past that:
+    lengths mixing runs of empty segments, 1-3 row segments, and lengths
+    on and around packet and run boundaries (2-8 rows a packet, 16-64 a
+    run), with enough rows that every lane holds several runs."""
+    torch = cuda
+    from helpers import program
+    rng = np.random.default_rng(41)
+    choices = np.array([0, 0, 1, 2, 3, 4, 5, 7, 8, 9, 15, 16, 17, 31, 32, 33, 63, 64, 65, 200, 1000])
+    lengths = rng.choice(choices, size=60_000)
+    lengths[100:400] = 0  # a long run of empty segments
+    offsets = offsets_of(lengths, index)
+    values = prepared(rng.normal(size=(int(offsets[-1]), d)), dtype)
+    tdtype = torch.float32 if dtype == "f32" else torch.bfloat16
+    prog = program(op, dtype, d, index)
+    out = torch.empty((offsets.size - 1, d), dtype=tdtype, device="cuda")
+    report = prog.run(torch.from_numpy(values).to(tdtype).to("cuda"), torch.from_numpy(offsets).to("cuda"), out,
+                      select="rowbalanced")
+    torch.cuda.synchronize()
+    assert "rowbalanced_packed" in report.kernel_names
+    check(out.float().cpu().numpy().astype(np.float64), values, offsets, op, dtype)
+
+
 @pytest.mark.parametrize("op", ["sum", "max", "softmax"])
 @pytest.mark.parametrize("dtype,d", [("f32", 3), ("bf16", 128), ("f32", 1024)])
 def test_classified_many_split_segments(cuda, op, dtype, d):
