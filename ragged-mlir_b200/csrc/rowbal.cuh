@@ -741,11 +741,15 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
   };
   // Staged rows are read from shared memory; rows outside this lane's
   // slice read as the operation's identity (0 for sum, -inf for max).
-  auto fold_row_if = [&](const float (&x)[E], int k, bool in) {
-    float row[DS];
+  // A pass folds its rows into two independent chains (even and odd rows
+  // of the run), merged into the accumulator at the end of the pass.
+  constexpr float kIdentity = OP == OP_MAX ? -kInf : 0.0f;
+  auto chain_fold = [&](float (&q)[DS], const float (&x)[E], int k, bool in) {
 #pragma unroll
-    for (int f = 0; f < DS; ++f) row[f] = in ? x[k * DS + f] : (OP == OP_MAX ? -kInf : 0.0f);
-    acc.fold_raw(row);
+    for (int f = 0; f < DS; ++f) {
+      const float v = in ? x[k * DS + f] : kIdentity;
+      q[f] = OP == OP_MAX ? max_nan(q[f], v) : __fadd_rn(q[f], v);
+    }
   };
 
   const uint4 *packets = reinterpret_cast<const uint4 *>(values);
@@ -797,13 +801,16 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
       // Fold staged rows [from, to) in one pass (predicated unless the pass
       // covers the whole run).
       auto pass = [&](int from, int to) {
+        float q[2][DS];
+#pragma unroll
+        for (int f = 0; f < DS; ++f) q[0][f] = q[1][f] = kIdentity;
         if (from == 0 && to == kRunRows) {
 #pragma unroll
           for (int k = 0; k < kPackedRun; ++k) {
             float x[E];
             VecIO<T, E>::unpack(*reinterpret_cast<const typename VecIO<T, E>::Raw *>(&mine[k]), x);
 #pragma unroll
-            for (int kk = 0; kk < R; ++kk) fold_row_if(x, kk, true);
+            for (int kk = 0; kk < R; ++kk) chain_fold(q[(k * R + kk) & 1], x, kk, true);
           }
         } else {
 #pragma unroll
@@ -811,9 +818,14 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
             float x[E];
             VecIO<T, E>::unpack(*reinterpret_cast<const typename VecIO<T, E>::Raw *>(&mine[k]), x);
 #pragma unroll
-            for (int kk = 0; kk < R; ++kk) fold_row_if(x, kk, k * R + kk >= from && k * R + kk < to);
+            for (int kk = 0; kk < R; ++kk)
+              chain_fold(q[(k * R + kk) & 1], x, kk, k * R + kk >= from && k * R + kk < to);
           }
         }
+        float merged[DS];
+#pragma unroll
+        for (int f = 0; f < DS; ++f) merged[f] = OP == OP_MAX ? max_nan(q[0][f], q[1][f]) : __fadd_rn(q[0][f], q[1][f]);
+        acc.fold_raw(merged);
         acc.account(to - from);
       };
       if (w2 >= hi) {
