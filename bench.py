@@ -546,7 +546,9 @@ def ours(args) -> None:
                             "end_weight_fit": split_fit,
                             "rank_ms": list(RANK_MS),
                             "collective": "NCCL all-gather of edge records",
-                            "edge_bytes_per_rank": _native_edge_bytes(w)}
+                            "edge_bytes_per_rank": _native_edge_bytes(w),
+                            "phases_ms": phase_profile(torch, dist, program, w, values, offsets, out, world, rank,
+                                                       splits, exchange, flush)}
     if not args.no_e2e:
         line["e2e"] = e2e_leg(torch, args, w, program, values, offsets_host, out, max_len, select, stream, dist,
                               splits, owners, rank, world, exchange)
@@ -563,6 +565,61 @@ def ours(args) -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def phase_profile(torch, dist, program, w, values, offsets, out, world, rank, splits, exchange, flush,
+                  steps: int = 5) -> dict:
+    """Per-rank device time of each phase of a sharded call, after the timed
+    steps (untimed for the headline): ``local`` (rg_run_shard: the window's
+    kernel and fix-up), ``exchange`` (the all-gather as the rank sees it,
+    waiting for the slowest rank included), ``combine`` (shard_combine), each
+    the median of ``steps`` calls with events around the phases; and
+    ``allgather_alone``: the same all-gather with the ranks' streams aligned
+    first, so its time is the collective's own."""
+    import statistics as st
+    marks = {}
+
+    def timed_exchange(edges):
+        marks["a"].record()
+        gathered = exchange(edges)
+        marks["b"].record()
+        return gathered
+
+    local, wait, combine, alone = [], [], [], []
+    align = torch.zeros(1, device=values.device)
+    for _ in range(steps):
+        if flush is not None:
+            flush()
+        dist.barrier()
+        torch.cuda.synchronize()
+        dist.all_reduce(align)
+        marks.update({k: torch.cuda.Event(enable_timing=True) for k in ("s", "a", "b", "e")})
+        marks["s"].record()
+        program.run_sharded(values, offsets, out, total_rows=w.n, world=world, rank=rank, exchange=timed_exchange,
+                            splits=splits)
+        marks["e"].record()
+        torch.cuda.synchronize()
+        local.append(marks["s"].elapsed_time(marks["a"]))
+        wait.append(marks["a"].elapsed_time(marks["b"]))
+        combine.append(marks["b"].elapsed_time(marks["e"]))
+    edges = torch.zeros(_native_edge_bytes(w) // 4, dtype=torch.float32, device=values.device)
+    for _ in range(steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        dist.all_reduce(align)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        exchange(edges)
+        end.record()
+        torch.cuda.synchronize()
+        alone.append(start.elapsed_time(end))
+    mine = torch.tensor([st.median(x) for x in (local, wait, combine, alone)], dtype=torch.float64,
+                        device=values.device)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    table = [[round(float(v), 4) for v in t.cpu().tolist()] for t in every]
+    return {name: [row[i] for row in table] for i, name in enumerate(("local", "exchange", "combine",
+                                                                      "allgather_alone"))}
 
 
 def refit_split(torch, dist, program, w, values, offsets, out, offsets_host, world, rank, splits, weight):

@@ -44,11 +44,11 @@ const void *kernel_ptr() {
       &rowbal_kernel<T, OffT, OP, VEC, RowbalTuning::kUnroll, RowbalTuning::kDoubleBuffer, minb_of(OP), XF>);
 }
 
-// Narrow rows that pack whole rows into 16-byte packets (2, 4 or 8 bytes a
-// row) take the packed kernel; VEC equals D for them.
+// Narrow rows that pack whole rows into 16-byte packets (2, 4, 8 or 16 bytes
+// a row) take the packed kernel; VEC equals D for them.
 bool packs(const Problem &p, const Geometry &g) {
   const int64_t row_bytes = p.d * elem_bytes(p.dtype);
-  return !(p.flags & RG_FLAG_NO_VECTORIZE) && row_bytes < 16 && 16 % row_bytes == 0 && g.vec == p.d;
+  return !(p.flags & RG_FLAG_NO_VECTORIZE) && row_bytes <= 16 && 16 % row_bytes == 0 && g.vec == p.d;
 }
 
 // The packed kernel, its staging area (above the 48 KB default of dynamic
@@ -56,7 +56,7 @@ bool packs(const Problem &p, const Geometry &g) {
 template <typename T, typename OffT, int OP, int VEC>
 const void *packed_ptr(int *status) {
   *status = RG_OK;
-  if constexpr (VEC * sizeof(T) < 16 && OP != OP_SOFTMAX) {
+  if constexpr (VEC * sizeof(T) <= 16 && OP != OP_SOFTMAX) {
     const void *kernel = reinterpret_cast<const void *>(&rowbal_packed_kernel<T, OffT, OP, VEC>);
     *status = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackedStageBytes),
                          "cudaFuncSetAttribute(rowbal_packed_kernel)");
@@ -144,7 +144,7 @@ int run_typed(const Problem &p, const Geometry &g, void *workspace, int64_t *byt
   }
   float *pieces = static_cast<float *>(workspace);
   UnitMeta *meta = reinterpret_cast<UnitMeta *>(static_cast<char *>(workspace) + plan.pieces_bytes);
-  if constexpr (VEC * sizeof(T) < 16 && OP != OP_SOFTMAX) {
+  if constexpr (VEC * sizeof(T) <= 16 && OP != OP_SOFTMAX) {
     if (packed && reinterpret_cast<uintptr_t>(p.values) % 16 == 0) {
       const int64_t ctas = plan.packed_ctas;
       dim3 grid(static_cast<unsigned>(ctas), 1, 1);

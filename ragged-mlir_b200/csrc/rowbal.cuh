@@ -34,7 +34,7 @@ namespace rgb {
 constexpr int kRowbalThreads = 256;
 constexpr int kRowbalSmem = 0;  // dynamic shared memory per CTA
 
-// Streaming knobs (measured on B200; see the tuning notes in DESIGN.md):
+// Streaming knobs, chosen by measurement on B200 (c1, c5):
 // U rows per register batch, DB = keep a second batch in flight while
 // folding, MINB = minimum resident CTAs per SM requested from ptxas.
 struct RowbalTuning {
@@ -646,7 +646,7 @@ rowbal_kernel(const T *__restrict__ values, const OffT *__restrict__ offsets, T 
   }
 }
 
-// Narrow rows (D * sizeof(T) in {2, 4, 8} bytes): every lane is a unit and
+// Narrow rows (D * sizeof(T) in {2, 4, 8, 16} bytes): every lane is a unit and
 // folds 16-byte packets of R = 16 / (D * sizeof(T)) whole rows, a packet at
 // once when no segment boundary falls inside it.  A warp finds its slice of
 // the merge path with a 32-ary search; each lane then finds its own slice by

@@ -38,7 +38,7 @@ END_WEIGHT = 1.25
 def end_weight_model(op: str, dtype: str, d: int) -> float:
     """Starting weight of a segment end, in rows: an end writes one output
     row and restarts the accumulators, about 128 bytes of streaming on B200
-    beyond the row (the round-1 hand fit for bf16 D=256: 1.25 rows), so
+    beyond the row (an earlier hand fit for bf16 D=256 gave 1.25 rows), so
     1 + 128 / row bytes.  Refined from measured rank times by
     ``fit_end_weight``."""
     row_bytes = d * (2 if dtype == "bf16" else 4)

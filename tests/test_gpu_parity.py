@@ -220,9 +220,10 @@ def test_validation_errors(cuda):
 
 
 @pytest.mark.parametrize("op", ["sum", "max"])
-@pytest.mark.parametrize("dtype,d", [("f32", 1), ("f32", 2), ("bf16", 1), ("bf16", 2), ("bf16", 4)])
+@pytest.mark.parametrize("dtype,d", [("f32", 1), ("f32", 2), ("f32", 4), ("bf16", 1), ("bf16", 2), ("bf16", 4),
+                                     ("bf16", 8)])
 def test_narrow_rows_packed_and_unaligned(cuda, op, dtype, d):
-    """Rows of 2-8 bytes: the packed kernel (16-byte aligned values) and
+    """Rows of 2-16 bytes: the packed kernel (16-byte aligned values) and
     the per-row kernel it falls back to for a view that is not."""
     torch = cuda
     from helpers import program
@@ -233,7 +234,8 @@ def test_narrow_rows_packed_and_unaligned(cuda, op, dtype, d):
     tdtype = torch.float32 if dtype == "f32" else torch.bfloat16
     prog = program(op, dtype, d, "i32")
     device_offsets = torch.from_numpy(offsets).to("cuda")
-    for shift in (0, 1):  # shift one row: misaligns the base for the packed loads
+    row_bytes = d * (4 if dtype == "f32" else 2)
+    for shift in (0, 1):  # shift one row: misaligns the base for the packed loads (rows under 16 bytes)
         base = torch.zeros((values.shape[0] + 1, d), dtype=tdtype, device="cuda")
         view = base[shift:shift + values.shape[0]]
         view.copy_(torch.from_numpy(values).to(tdtype))
@@ -242,14 +244,14 @@ def test_narrow_rows_packed_and_unaligned(cuda, op, dtype, d):
         torch.cuda.synchronize()
         check(out.float().cpu().numpy().astype(np.float64), values, offsets, op, dtype)
         names = set(report.kernel_names)
-        if shift == 0:
+        if shift == 0 or row_bytes == 16:
             assert "rowbalanced_packed" in names
         else:
             assert "rowbalanced" in names and "rowbalanced_packed" not in names
 
 
 @pytest.mark.parametrize("op", ["sum", "max"])
-@pytest.mark.parametrize("dtype,d", [("f32", 1), ("f32", 2), ("bf16", 1), ("bf16", 4)])
+@pytest.mark.parametrize("dtype,d", [("f32", 1), ("f32", 2), ("f32", 4), ("bf16", 1), ("bf16", 4), ("bf16", 8)])
 @pytest.mark.parametrize("index", ["i32", "i64"])
 def test_packed_segment_ends_inside_staged_runs(cuda, op, dtype, d, index):
     """The packed kernel folds a staged run of 8 packets in one pass per
