@@ -61,6 +61,7 @@ constexpr int kPipeTeams = kPipeConsumerWarps / kPipeTeamWarps;
 constexpr int kPipeThreads = 32 * (kPipeConsumerWarps + 1);
 constexpr int kPipeProducer = kPipeConsumerWarps;  // warp index of the producer
 constexpr int kPipeClaim = 32;                     // segments claimed per atomic
+constexpr int kGroupRows = 32;                     // run segments up to this many rows: one lane group each
 #ifndef RG_PIPE_SMEM_KB
 #define RG_PIPE_SMEM_KB 227
 #endif
@@ -379,13 +380,41 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       // quarter of the run's rows holds the segment's middle row, so the
       // warps get contiguous groups of segments with about equal rows.
       const int64_t r0 = r.r0, span = r.r1 - r.r0;
-      int64_t begin = r0;
       const int count = r.count;
+      // Segments of at most kGroupRows rows go to single lane groups (group
+      // g of the team takes run segments g, g + groups, ...): a group holds
+      // whole rows, so it needs no merge with other groups, and the warp
+      // works on 32 / G segments at once.
+      // (Not with the fused transform: its register budget is spent.)
+      constexpr int64_t kGroupMax = XF ? -1 : kGroupRows;
+      const int groups = kPipeTeamWarps << (5 - a.g_shift);
+      for (int k = XF ? count : static_cast<int>(team_lane); k < count; k += groups) {
+        const int64_t begin = k ? r.ends[k - 1] : r0, end = r.ends[k];
+        if (end - begin > kGroupMax || !active) continue;
+        Acc<OP, VEC> acc;
+        acc.init();
+        if constexpr (OP == OP_SOFTMAX) {
+          float base[VEC], mine[VEC], ref[VEC], inv[VEC], f[VEC];
+          staged_stats_keep<T, VEC, XF>(acc, rows, begin, end, 0, 1, base, a.xform, col);
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) mine[v] = acc.st[v].r;
+          stats_of<VEC>(acc, ref, inv);
+          kept_factor<VEC>(base, mine, ref, inv, f);
+          normalize_kept<T, VEC>(rows, out, d, col, begin, end, 0, 1, f);
+        } else {
+          fold_staged<T, OP, VEC>(acc, rows, begin, end, 0, 1);
+          float y[VEC];
+          acc.result(y);
+          VecIO<T, VEC>::store(out + (r.seg + k) * d + col, y);
+        }
+      }
+      // Longer segments: one warp each.
+      int64_t begin = r0;
       for (int k = 0; k < count; ++k) {
         const int64_t end = r.ends[k];
         const int64_t seg = r.seg + k;
         const int owner = span > 0 ? static_cast<int>(((begin + end - 2 * r0) * kPipeTeamWarps) / (2 * span)) : 0;
-        if ((owner < kPipeTeamWarps ? owner : kPipeTeamWarps - 1) == wit) {
+        if (end - begin > kGroupMax && (owner < kPipeTeamWarps ? owner : kPipeTeamWarps - 1) == wit) {
           Acc<OP, VEC> acc;
           acc.init();
           if constexpr (OP == OP_SOFTMAX) {
