@@ -15,9 +15,10 @@ public API (CUDA events around complete calls, median of 5 after 2 warm-up
 calls, L2 flushed before each call when the inputs are smaller than 4x L2).
 ``fit`` fits, per operation family and schedule, the six nonnegative
 coefficients of ``selection.features`` that minimise the squared relative
-error on the training group (NNLS on rows scaled by 1/time), and picks the
+error on the training group (NNLS on rows scaled by 1/time), picks the
 margin in 0..10% that puts the most training cases within 3% of their
-fastest schedule.  ``evaluate`` reports, on the held-out group, the share of
+fastest schedule, and fits the tree chooser (``fit_chooser``) that makes
+the version-4 model's choice.  ``evaluate`` reports, on the held-out group, the share of
 cases whose chosen schedule is within 3% of the fastest one measured.  The
 L2 capacity of the bytes-beyond-L2 term is the measuring device's.
 """
@@ -32,7 +33,8 @@ import sys
 
 import numpy as np
 
-from .selection import FAMILIES, MODEL_PATH, TERMS, CostModel, family, features
+from .selection import (CHOICE_FEATURES, FAMILIES, MODEL_PATH, SCHEDULES, TERMS, CostModel, TreeChooser,
+                        choice_features, family, features)
 
 DISTRIBUTIONS = ("uniform", "long_tail", "bimodal", "burst", "exponential")
 WITHIN = 0.03
@@ -159,6 +161,63 @@ def fit_coefficients(cases: list[dict], l2_mib: float) -> dict:
     return coefficients
 
 
+def _choice_row(case: dict) -> np.ndarray:
+    element = 4 if case["dtype"] == "f32" else 2
+    return choice_features(case["op"], case["n"], case["b"], case["d"], case["max_len"], element)
+
+
+def fit_chooser(cases: list[dict], *, rounds: int = 100, leaves: int = 15, seed: int = 0) -> dict:
+    """Gradient-boosted trees (scikit-learn's histogram boosting, fit time
+    only) predicting each training case's fastest schedule from
+    ``choice_features``, exported as the node arrays of
+    ``selection.TreeChooser``.  The export is checked against scikit-learn's
+    own predictions on every case, and a sample of them is recorded as
+    ``checks`` that loading the model replays."""
+    from sklearn.ensemble import HistGradientBoostingClassifier
+    x = np.array([_choice_row(c) for c in cases])
+    y = np.array([min(c["times_us"], key=c["times_us"].get) for c in cases])
+    model = HistGradientBoostingClassifier(max_iter=rounds, max_leaf_nodes=leaves, learning_rate=0.1,
+                                           early_stopping=False, random_state=seed)
+    model.fit(x, y)
+    classes = [str(c) for c in model.classes_]
+    feature, threshold, left, right, value, leaf, roots, tree_class = [], [], [], [], [], [], [], []
+    max_depth = 0
+    for trees in model._predictors:  # one list per boosting round: a tree per class
+        if len(trees) != len(classes):
+            raise RuntimeError("expected one tree per class and round")
+        for k, tree in enumerate(trees):
+            base = len(feature)
+            nodes = tree.nodes
+            if np.any(nodes["is_categorical"]):  # the features are never missing, so only numeric splits matter
+                raise RuntimeError("categorical splits are not exported")
+            roots.append(base)
+            tree_class.append(k)
+            max_depth = max(max_depth, int(nodes["depth"].max()))
+            for node in nodes:
+                is_leaf = bool(node["is_leaf"])
+                feature.append(0 if is_leaf else int(node["feature_idx"]))
+                threshold.append(0.0 if is_leaf else float(node["num_threshold"]))
+                left.append(base + int(node["left"]) if not is_leaf else -1)
+                right.append(base + int(node["right"]) if not is_leaf else -1)
+                value.append(float(node["value"]) if is_leaf else 0.0)
+                leaf.append(is_leaf)
+    baseline = np.asarray(model._baseline_prediction, dtype=np.float64).reshape(-1)
+    if len(classes) == 2:
+        raise RuntimeError("the export expects three or more schedules (one tree per class)")
+    data = {"features": CHOICE_FEATURES, "classes": classes, "baseline": [float(v) for v in baseline],
+            "nodes": {"feature": feature, "threshold": threshold, "left": left, "right": right, "value": value,
+                      "leaf": leaf},
+            "roots": roots, "tree_class": tree_class, "max_depth": max_depth}
+    chooser = TreeChooser.from_dict(data)
+    expected = model.predict(x)
+    mine = [chooser.classes[int(np.argmax(chooser.scores(row)))] for row in x]
+    if any(a != b for a, b in zip(mine, expected)):
+        raise RuntimeError("exported trees disagree with scikit-learn's predictions")
+    step = max(1, len(x) // 32)
+    data["checks"] = [[float(v) for v in x[i]] + [str(expected[i])] for i in range(0, len(x), step)]
+    return data
+
+
 def within_share(model: CostModel, cases: list[dict], l2_mib: float) -> tuple[int, int, list[dict]]:
     hits, misses = 0, []
     for case in cases:
@@ -177,6 +236,15 @@ def within_share(model: CostModel, cases: list[dict], l2_mib: float) -> tuple[in
     return hits, len(cases), misses
 
 
+def _slowdown(model: CostModel, case: dict, l2_mib: float) -> float:
+    from .optimizations import Optimizations
+    tile, vec = Optimizations().geometry(case["d"], case["dtype"])
+    element = 4 if case["dtype"] == "f32" else 2
+    chosen, _ = model.choose(case["op"], case["n"], case["b"], case["d"], case["max_len"], tile * vec, element,
+                             l2_mib=l2_mib, available=tuple(case["times_us"]))
+    return case["times_us"][chosen] / min(case["times_us"].values())
+
+
 def fit(args: argparse.Namespace) -> None:
     data = json.loads(Path(args.runs).read_text())
     l2_mib = float(data["l2_mib"])
@@ -189,14 +257,25 @@ def fit(args: argparse.Namespace) -> None:
         hits, _, _ = within_share(model, train, l2_mib)
         if hits > best_hits:
             best_margin, best_hits = margin, hits
-    model = CostModel(coefficients, best_margin, {}, l2_mib)
+    linear = CostModel(coefficients, best_margin, {}, l2_mib)
+    linear_held, _, _ = within_share(linear, heldout, l2_mib)
+    chooser = fit_chooser(train)
+    model = CostModel(coefficients, best_margin, {}, l2_mib, TreeChooser.from_dict(chooser))
+    train_hits, _, _ = within_share(model, train, l2_mib)
     held_hits, held_total, held_misses = within_share(model, heldout, l2_mib)
-    out = {"version": 3, "coefficients": coefficients, "margin": best_margin, "l2_mib": l2_mib,
+    slowdowns = [_slowdown(model, c, l2_mib) for c in heldout]
+    out = {"version": 4, "coefficients": coefficients, "margin": best_margin, "l2_mib": l2_mib, "chooser": chooser,
            "calibration": {"status": "fitted by python -m ragged.calibrate fit", "device": data["device"],
                            "runs": Path(args.runs).name, "train_cases": len(train), "heldout_cases": held_total,
-                           "train_within_3pct": best_hits, "heldout_within_3pct": held_hits,
-                           "heldout_share": round(held_hits / max(1, held_total), 4)}}
-    Path(args.output).write_text(json.dumps(out, indent=2) + "\n")
+                           "train_within_3pct": train_hits, "heldout_within_3pct": held_hits,
+                           "heldout_share": round(held_hits / max(1, held_total), 4),
+                           "heldout_geomean_slowdown": round(float(np.exp(np.mean(np.log(slowdowns)))), 4),
+                           "heldout_worst_slowdown": round(max(slowdowns), 3),
+                           "linear_only_heldout_share": round(linear_held / max(1, held_total), 4)}}
+    # The tree arrays go on one line; the rest stays readable.
+    text = json.dumps({**out, "chooser": "@chooser@"}, indent=2)
+    text = text.replace('"@chooser@"', json.dumps(chooser, separators=(",", ":")))
+    Path(args.output).write_text(text + "\n")
     print(json.dumps(out["calibration"]))
     for miss in held_misses:
         print("held-out miss:", json.dumps(miss))

@@ -45,3 +45,30 @@ def test_suite_is_seeded_and_split():
     for distribution in calibrate.DISTRIBUTIONS:
         lengths = calibrate.lengths_of(distribution, 100, 10_000, np.random.default_rng(1))
         assert lengths.sum() == 10_000 and (lengths >= 0).all()
+
+
+def test_tree_chooser_fit_reproduces_its_labels():
+    """A fastest schedule that depends on N and D only: the exported trees
+    agree with scikit-learn (fit_chooser raises otherwise), replay their
+    recorded checks on load, and choose the fastest schedule on held-out
+    cases of the same rule."""
+    from ragged.selection import TreeChooser
+
+    def runs(seed, count):
+        cases = []
+        for case in calibrate.suite(seed=seed, count=count):
+            case = dict(case, max_len=max(1, case["n"] // max(1, case["b"]) * 3))
+            small, wide = case["n"] < 2**16, case["d"] >= 256
+            best = "naive" if small else ("classified" if wide else "rowbalanced")
+            case["times_us"] = {s: (10.0 if s == best else 20.0) for s in ("classified", "naive", "rowbalanced")}
+            cases.append(case)
+        return cases
+
+    train, heldout = runs(11, 400), runs(12, 120)
+    data = calibrate.fit_chooser(train, rounds=30)
+    chooser = TreeChooser.from_dict(data)
+    assert data["checks"] and chooser.max_depth >= 1
+    fitted = calibrate.fit_coefficients(train, 126.0)
+    model = CostModel(fitted, 0.0, {}, 126.0, chooser)
+    hits, total, misses = calibrate.within_share(model, heldout, 126.0)
+    assert hits >= 0.95 * total, misses

@@ -144,6 +144,50 @@ def test_cost_model_terms_and_choice():
 def test_shipped_cost_model_loads():
     model = selection.default_model()
     assert set(model.coefficients) == {"reduce", "softmax"}
+    assert model.chooser is not None and set(model.chooser.classes) == {"classified", "naive", "rowbalanced"}
+    assert model.calibration["heldout_share"] >= 0.9  # the calibration run's held-out group (B200)
+
+
+def _chooser_dict(**overrides):
+    """Three one-split trees: naive scores +1 when log2(N) <= 10, else -1;
+    the other schedules score 0 (one leaf each)."""
+    data = {"features": selection.CHOICE_FEATURES, "classes": ["classified", "naive", "rowbalanced"],
+            "baseline": [0.0, 0.0, 0.0],
+            "nodes": {"feature": [0, 0, 0, 0, 0], "threshold": [0.0, 10.0, 0.0, 0.0, 0.0],
+                      "left": [-1, 2, -1, -1, -1], "right": [-1, 3, -1, -1, -1],
+                      "value": [0.0, 0.0, 1.0, -1.0, 0.0], "leaf": [True, False, True, True, True]},
+            "roots": [0, 1, 4], "tree_class": [0, 1, 2], "max_depth": 1}
+    data.update(overrides)
+    return data
+
+
+def test_tree_chooser_choice_and_validation():
+    linear = {"reduce": {s: [10, 0, 0, 0, 0, 0] for s in ("classified", "naive", "rowbalanced")},
+              "softmax": {s: [10, 0, 0, 0, 0, 0] for s in ("classified", "naive")}}
+    model = selection.CostModel.from_dict({"version": 4, "margin": 0.0, "l2_mib": 100.0, "coefficients": linear,
+                                           "chooser": _chooser_dict()})
+    assert model.choose("sum", 512, 4, 8, 128, 8)[0] == "naive"            # log2(512) = 9 <= 10
+    choice, details = model.choose("sum", 1 << 20, 4, 8, 128, 8)
+    assert choice == "rowbalanced" and details["scores"]["naive"] == -1.0  # ties go to the family default
+    assert model.choose("softmax", 1 << 20, 4, 8, 128, 8)[0] == "classified"
+    assert model.choose("sum", 512, 4, 8, None, 8)[0] == "rowbalanced"     # no length statistics
+    assert model.choose("sum", 512, 4, 8, 128, 8, available=("classified", "rowbalanced"))[0] == "rowbalanced"
+    checks = [list(selection.choice_features("sum", 512, 4, 8, 128, 4)) + ["naive"]]
+    selection.TreeChooser.from_dict(_chooser_dict(checks=checks))
+    bad = [
+        _chooser_dict(checks=[checks[0][:-1] + ["classified"]]),               # recorded choice not reproduced
+        _chooser_dict(features="other"),
+        _chooser_dict(classes=["classified", "naive", "naive"]),
+        _chooser_dict(roots=[0, 1, 9]),
+        _chooser_dict(nodes={**_chooser_dict()["nodes"], "left": [-1, 7, -1, -1, -1]}),
+        _chooser_dict(nodes={**_chooser_dict()["nodes"], "feature": [0, 99, 0, 0, 0]}),
+        _chooser_dict(baseline=[0.0, 0.0]),
+    ]
+    for data in bad:
+        with pytest.raises(CacheMismatch):
+            selection.TreeChooser.from_dict(data)
+    with pytest.raises(CacheMismatch):
+        selection.CostModel.from_dict({"version": 4, "margin": 0.0, "l2_mib": 1.0, "coefficients": linear})
 
 
 @pytest.mark.parametrize("name", workloads.CONFIGS)
