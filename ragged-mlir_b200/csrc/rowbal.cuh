@@ -840,13 +840,20 @@ rowbal_packed_kernel(const T *__restrict__ values, const OffT *__restrict__ offs
           cur = stop;
         }
       } else {
-        // Three or more ends inside: row by row.
+        // Three or more ends inside: each piece between them row by row
+        // (plain adds into the block, counted once per piece).
         const T *const rows = reinterpret_cast<const T *>(mine);
-        for (int i = a; i < e; ++i) {
-          while (w0 <= run_row + i) finish();
-          float x[DS];
-          VecIO<T, DS>::unpack(*reinterpret_cast<const typename VecIO<T, DS>::Raw *>(rows + i * DS), x);
-          acc.fold(x);
+        for (int cur = a;;) {
+          const int stop = w0 < hi ? static_cast<int>(w0 - run_row) : e;
+          for (int i = cur; i < stop; ++i) {
+            float x[DS];
+            VecIO<T, DS>::unpack(*reinterpret_cast<const typename VecIO<T, DS>::Raw *>(rows + i * DS), x);
+            acc.fold_raw(x);
+          }
+          acc.account(stop - cur);
+          if (stop == e) break;
+          do finish(); while (w0 <= run_row + stop);
+          cur = stop;
         }
       }
     }
