@@ -172,6 +172,7 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
   a.late = reinterpret_cast<unsigned *>(ws + l.late);
   a.wait_polls = chunk_wait_polls();
   a.xform = xf;
+  a.claim = kPipeClaim;
 
   // The pipelined worker's grid (one resident wave).  Softmax split segments
   // of at most min(kWaitChunks, ctas / 2) chunks are normalised by the
@@ -189,6 +190,9 @@ int launch_typed(const Problem &p, const Geometry &g, char *ws, cudaStream_t str
     const int64_t max_items = (p.b + kPipeClaim - 1) / kPipeClaim + l.chunks;
     if (pipe_ctas > max_items) pipe_ctas = max_items;
     if (pipe_ctas < 1) pipe_ctas = 1;
+    // Many segments per CTA (8 claims of kRunMax each or more): claims of
+    // kRunMax segments, so runs of short segments fill more of a stage.
+    if (p.b >= pipe_ctas * 8 * kRunMax) a.claim = kRunMax;
     if constexpr (OP == OP_SOFTMAX) {
       const int64_t wait_chunks = pipe_ctas / 2 < kWaitChunks ? pipe_ctas / 2 : kWaitChunks;
       a.wait_rows = wait_chunks * a.item_rows;

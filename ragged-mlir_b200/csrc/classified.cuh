@@ -263,6 +263,7 @@ struct ClsArgs {
   int64_t wait_rows;   // softmax split segments up to this length are normalised by the worker (0: none)
   unsigned *late;      // softmax: [chunks] nonzero = chunk whose wait gave up (normalised by split_normalize)
   int wait_polls;      // polls before a wait gives up
+  int claim;           // pipelined worker: segments per producer claim (kPipeClaim or kRunMax)
   Xform xform;         // softmax input transform fused into the loads (pipelined worker, normalise kernel)
 };
 

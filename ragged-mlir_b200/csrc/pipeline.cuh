@@ -60,7 +60,8 @@ static_assert((kPipeTeamWarps & (kPipeTeamWarps - 1)) == 0, "warps per team must
 constexpr int kPipeTeams = kPipeConsumerWarps / kPipeTeamWarps;
 constexpr int kPipeThreads = 32 * (kPipeConsumerWarps + 1);
 constexpr int kPipeProducer = kPipeConsumerWarps;  // warp index of the producer
-constexpr int kPipeClaim = 32;                     // segments claimed per atomic
+constexpr int kPipeClaim = 32;                     // segments claimed per atomic (calls with few segments per CTA)
+constexpr int kRunMax = 128;                       // segments per run (and per claim of calls with many)
 constexpr int kGroupRows = 32;                     // run segments up to this many rows: one lane group each
 #ifndef RG_PIPE_SMEM_KB
 #define RG_PIPE_SMEM_KB 227
@@ -88,7 +89,7 @@ struct StageRecord {
   int32_t chunk_first, chunk_last;  // SPLIT: this stage starts / ends its chunk
   int32_t wait;        // SPLIT (softmax): the team waits for the segment and normalises the stage
   int32_t pad2;
-  int64_t ends[kPipeClaim];      // RUN: end row of each segment of the run
+  int32_t ends[kRunMax];         // RUN: end row of each segment of the run, relative to r0
 };
 
 // Shared memory: the stages, their records, the barriers and, for softmax,
@@ -214,62 +215,102 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
         bulk_copy_g2s(dst + at, static_cast<const char *>(src) + at, n, &full[s]);
       }
     };
-    // Runs of consecutive short segments, 32 segments per claim.  Claims are
-    // prefetched: while the stages of claim k are published, the atomic of
-    // claim k + 2 and the offsets of claim k + 1 are in flight.
-    auto claim_offsets = [&](int64_t base, int64_t &o0, int64_t &o1) {
-      const int64_t sg = base + lane;
-      o0 = sg < a.b ? static_cast<int64_t>(offsets[sg]) : 0;
-      o1 = sg < a.b ? static_cast<int64_t>(offsets[sg + 1]) : 0;
+    // Runs of consecutive short segments.  A claim is a.claim segments (32,
+    // or kRunMax when the call has many segments per CTA), read as
+    // sub-batches of 32, one per lane; a run may continue across the
+    // sub-batches of its claim up to kRunMax segments and one stage of
+    // rows.  Claims are prefetched: while the stages of claim k are
+    // published, the atomic of claim k + 2 and the offsets of claim k + 1
+    // are in flight.
+    constexpr int kSub = kRunMax / 32;
+    auto claim_offsets = [&](int64_t base, int64_t (&c0)[kSub], int64_t (&c1)[kSub]) {
+#pragma unroll
+      for (int q = 0; q < kSub; ++q) {
+        const int64_t sg = base + q * 32 + lane;
+        const bool v = q * 32 < a.claim && sg < a.b;
+        c0[q] = v ? static_cast<int64_t>(offsets[sg]) : 0;
+        c1[q] = v ? static_cast<int64_t>(offsets[sg + 1]) : 0;
+      }
     };
     int team = 0;  // team of the next stage (runs) or chunk (split)
     unsigned long long pending = 0;
-    if (lane == 0) pending = atomicAdd(&a.state->work, static_cast<unsigned long long>(kPipeClaim));
+    const unsigned long long claim = static_cast<unsigned long long>(a.claim);
+    if (lane == 0) pending = atomicAdd(&a.state->work, claim);
     int64_t base = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
-    if (lane == 0 && base < a.b) pending = atomicAdd(&a.state->work, static_cast<unsigned long long>(kPipeClaim));
-    int64_t o0 = 0, o1 = 0;
-    if (base < a.b) claim_offsets(base, o0, o1);
+    if (lane == 0 && base < a.b) pending = atomicAdd(&a.state->work, claim);
+    int64_t c0[kSub], c1[kSub];
+    if (base < a.b) claim_offsets(base, c0, c1);
     while (base < a.b) {
       const int64_t next = static_cast<int64_t>(__shfl_sync(0xffffffffu, pending, 0));
-      if (lane == 0 && next < a.b) pending = atomicAdd(&a.state->work, static_cast<unsigned long long>(kPipeClaim));
-      int64_t n0 = 0, n1 = 0;
+      if (lane == 0 && next < a.b) pending = atomicAdd(&a.state->work, claim);
+      int64_t n0[kSub], n1[kSub];
       if (next < a.b) claim_offsets(next, n0, n1);
-      const bool valid = base + lane < a.b;
-      const bool is_long = valid && (o1 - o0) > a.item_rows;
-      const unsigned valid_mask = __ballot_sync(0xffffffffu, valid);
-      const unsigned long_mask = __ballot_sync(0xffffffffu, is_long);
-      int i = 0;
-      while (i < 32 && ((valid_mask >> i) & 1u)) {
-        if ((long_mask >> i) & 1u) {
-          ++i;
-          continue;
-        }
-        // Extend the run from segment i while segments are short and the
-        // rows fit one stage.
-        const int64_t start = __shfl_sync(0xffffffffu, o0, i);
-        const bool stop = lane >= i && (!valid || is_long || o1 - start > a.item_rows);
-        const unsigned stop_mask = __ballot_sync(0xffffffffu, stop) & (~0u << i);
-        const int j = stop_mask ? __ffs(stop_mask) - 1 : 32;  // first segment not in the run
-        const int64_t end = __shfl_sync(0xffffffffu, o1, j - 1);
-        int s;
-        acquire(s);
-        StageRecord &r = rec[s];
+      // The open run: stage so, rows [run_start, run_end), run_count segments from run_seg.
+      bool open = false;
+      int so = 0, run_count = 0;
+      int64_t run_start = 0, run_end = 0, run_seg = 0;
+      auto close_run = [&]() {
         if (lane == 0) {
+          StageRecord &r = rec[so];
           r.kind = STAGE_RUN;
           r.team = team;
-          r.count = j - i;
-          r.seg = base + i;
-          r.r0 = start;
-          r.r1 = end;
+          r.count = run_count;
+          r.seg = run_seg;
+          r.r0 = run_start;
+          r.r1 = run_end;
         }
         team = team + 1 == kPipeTeams ? 0 : team + 1;
-        if (lane >= i && lane < j) r.ends[lane - i] = o1;
-        publish(s, values + start * d, static_cast<uint32_t>((end - start) * a.row_bytes));
-        i = j;
+        publish(so, values + run_start * d, static_cast<uint32_t>((run_end - run_start) * a.row_bytes));
+        open = false;
+      };
+#pragma unroll
+      for (int q = 0; q < kSub; ++q) {
+        const int64_t sb = base + q * 32;
+        if (q * 32 >= a.claim || sb >= a.b) break;
+        const int64_t o0 = c0[q], o1 = c1[q];
+        const bool valid = sb + lane < a.b;
+        const bool is_long = valid && (o1 - o0) > a.item_rows;
+        const unsigned valid_mask = __ballot_sync(0xffffffffu, valid);
+        const unsigned long_mask = __ballot_sync(0xffffffffu, is_long);
+        int i = 0;
+        while (i < 32 && ((valid_mask >> i) & 1u)) {
+          if ((long_mask >> i) & 1u) {
+            if (open) close_run();
+            ++i;
+            continue;
+          }
+          // Extend the open run (or a new one from segment i) while segments
+          // are short, the rows fit one stage and the record has room.
+          const int64_t start = open ? run_start : __shfl_sync(0xffffffffu, o0, i);
+          const int room = kRunMax - (open ? run_count : 0);
+          const bool stop = lane >= i && (!valid || is_long || o1 - start > a.item_rows || lane - i >= room);
+          const unsigned stop_mask = __ballot_sync(0xffffffffu, stop) & (~0u << i);
+          const int j = stop_mask ? __ffs(stop_mask) - 1 : 32;  // first segment not in the run
+          if (j == i) {
+            // Segment i does not fit the open run (a new run always takes it).
+            if (open) close_run(); else ++i;
+            continue;
+          }
+          if (!open) {
+            acquire(so);
+            open = true;
+            run_start = start;
+            run_seg = sb + i;
+            run_count = 0;
+          }
+          if (lane >= i && lane < j) rec[so].ends[run_count + lane - i] = static_cast<int32_t>(o1 - run_start);
+          run_end = __shfl_sync(0xffffffffu, o1, j - 1);
+          run_count += j - i;
+          i = j;
+        }
       }
+      if (open) close_run();
       base = next;
-      o0 = n0;
-      o1 = n1;
+#pragma unroll
+      for (int q = 0; q < kSub; ++q) {
+        c0[q] = n0[q];
+        c1[q] = n1[q];
+      }
     }
     // Split chunks in chunk order, one per atomic, claimed only once the
     // stage for it is held (a claimed chunk always reaches its team: the
@@ -389,7 +430,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
       constexpr int64_t kGroupMax = XF ? -1 : kGroupRows;
       const int groups = kPipeTeamWarps << (5 - a.g_shift);
       for (int k = XF ? count : static_cast<int>(team_lane); k < count; k += groups) {
-        const int64_t begin = k ? r.ends[k - 1] : r0, end = r.ends[k];
+        const int64_t begin = k ? r0 + r.ends[k - 1] : r0, end = r0 + r.ends[k];
         if (end - begin > kGroupMax || !active) continue;
         Acc<OP, VEC> acc;
         acc.init();
@@ -408,13 +449,17 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
           VecIO<T, VEC>::store(out + (r.seg + k) * d + col, y);
         }
       }
-      // Longer segments: one warp each.
-      int64_t begin = r0;
+      // Longer segments: one warp each (relative rows fit 32 bits: a run is
+      // at most one stage).
+      int begin_rel = 0;
+      const int span32 = static_cast<int>(span);
       for (int k = 0; k < count; ++k) {
-        const int64_t end = r.ends[k];
+        const int end_rel = r.ends[k];
+        const int64_t begin = r0 + begin_rel, end = r0 + end_rel;
         const int64_t seg = r.seg + k;
-        const int owner = span > 0 ? static_cast<int>(((begin + end - 2 * r0) * kPipeTeamWarps) / (2 * span)) : 0;
-        if (end - begin > kGroupMax && (owner < kPipeTeamWarps ? owner : kPipeTeamWarps - 1) == wit) {
+        const bool big = end_rel - begin_rel > kGroupMax;
+        const int owner = big && span32 > 0 ? ((begin_rel + end_rel) * kPipeTeamWarps) / (2 * span32) : 0;
+        if (big && (owner < kPipeTeamWarps ? owner : kPipeTeamWarps - 1) == wit) {
           Acc<OP, VEC> acc;
           acc.init();
           if constexpr (OP == OP_SOFTMAX) {
@@ -441,7 +486,7 @@ pipe_worker_kernel(const T *__restrict__ values, const OffT *__restrict__ offset
             }
           }
         }
-        begin = end;
+        begin_rel = end_rel;
       }
     } else if (kind == STAGE_SPLIT && r.team == team) {
       // ---- split chunk: one team folds the chunk's stages, publishes an

@@ -99,11 +99,13 @@ def test_c5_tenth_takes_the_claim_counter_path(cuda):
 
 
 @pytest.mark.parametrize("op", ["sum", "max"])
-def test_forty_million_row_segment_chains_thousands_of_virtual_ctas(cuda, op):
-    """f32 D=4 (one 16-byte vector a row, 256 units per CTA): 64M rows with
-    one 40M-row segment between short ones; the path is long enough for
+@pytest.mark.parametrize("d", [4, 8])
+def test_forty_million_row_segment_chains_thousands_of_virtual_ctas(cuda, op, d):
+    """64M rows with one 40M-row segment between short ones.  f32 D=8 (two
+    16-byte vectors a row, 128 units per CTA): the path is long enough for
     eight virtual CTAs per resident CTA, so the segment's fix-up chain
-    crosses thousands of them."""
+    crosses thousands of them.  f32 D=4 (one 16-byte packet a row): the
+    packed kernel's single wave, the chain crossing most of its CTAs."""
     rng = np.random.default_rng(40)
     short = rng.integers(0, 64, size=200_000)
     giant = 40_000_000
@@ -113,14 +115,17 @@ def test_forty_million_row_segment_chains_thousands_of_virtual_ctas(cuda, op):
     n, b = int(offsets_host[-1]), lengths.size
     g = cuda.Generator(device="cuda")
     g.manual_seed(4040)
-    values = cuda.empty((n, 4), dtype=cuda.float32, device="cuda").normal_(generator=g)
+    values = cuda.empty((n, d), dtype=cuda.float32, device="cuda").normal_(generator=g)
     if op == "max":
-        values[cuda.rand((n, 4), generator=g, device="cuda") < 1e-7] = float("nan")
-    program = _program(op, "f32", 4, "i64")
-    out = cuda.full((b, 4), -64.0, dtype=cuda.float32, device="cuda")
+        values[cuda.rand((n, d), generator=g, device="cuda") < 1e-7] = float("nan")
+    program = _program(op, "f32", d, "i64")
+    out = cuda.full((b, d), -64.0, dtype=cuda.float32, device="cuda")
     report = program.run(values, cuda.from_numpy(offsets_host).to("cuda"), out, select="rowbalanced")
     cuda.cuda.synchronize()
-    assert _claims(report)
     names = list(report.kernel_names)
-    assert report.grids[names.index("rowbalanced_fixup")][0] >= 2000
+    if d == 8:
+        assert _claims(report)
+        assert report.grids[names.index("rowbalanced_fixup")][0] >= 2000
+    else:
+        assert "rowbalanced_packed" in names
     dc.check_reduction(host_rows(out), fetcher(values), n, offsets_host, np.arange(b), op=op, dtype="f32")

@@ -278,6 +278,28 @@ def test_packed_segment_ends_inside_staged_runs(cuda, op, dtype, d, index):
 
 
 @pytest.mark.parametrize("op", ["sum", "max", "softmax"])
+@pytest.mark.parametrize("dtype,d", [("bf16", 8), ("f32", 16)])
+def test_classified_many_short_segments_long_claims(cuda, op, dtype, d):
+    """Enough segments per CTA that the pipelined worker's producer claims
+    128 segments at a time and runs continue across its 32-segment
+    sub-batches: lengths 0-3 with runs of empty segments, a few segments
+    longer than a stage (they end a run) and a final partial claim."""
+    from oracle import native
+    rng = np.random.default_rng(52)
+    count = 200_003
+    lengths = rng.integers(0, 4, size=count)
+    lengths[rng.integers(0, count, size=40)] = 3000  # split class: closes the open run
+    lengths[1000:1400] = 0
+    offsets = offsets_of(lengths, "i64")
+    values = prepared(rng.normal(size=(int(offsets[-1]), d)), dtype)
+    actual, report = run_device(cuda, op, dtype, values, offsets, select="classified")
+    assert "classified_worker" in report.kernel_names
+    reference = native.run(op, values, offsets, dtype=dtype)
+    scale = native.segment_reduce(values, offsets, "abssum", dtype=dtype) if op == "sum" else None
+    native.check(actual, op, dtype, offsets, reference, scale)
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "softmax"])
 @pytest.mark.parametrize("dtype,d", [("f32", 3), ("bf16", 128), ("f32", 1024)])
 def test_classified_many_split_segments(cuda, op, dtype, d):
     """Dozens of split-class segments (several chunks each, one ending on a
