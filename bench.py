@@ -483,9 +483,10 @@ def ours(args) -> None:
     flush = (lambda: flush_l2(flush_buffer)) if flush_buffer is not None else None
     report_holder = {}
     exchange = torch_exchange() if world > 1 else None
-    if world >= 4 and not args.no_split_fit:
+    if world > 1 and not args.no_split_fit:
         # Refit the split from measured local phases (the shard kernel and its
-        # fix-up on each rank's rows, exchange left out), then re-shard.
+        # fix-up on each rank's rows, exchange left out), then re-shard (the
+        # fit needs four ranks or more; with fewer the model weight stays).
         end_weight, split_fit, splits = refit_split(torch, dist, program, w, values, offsets, out, offsets_host,
                                                     world, rank, splits, end_weight)
         new_rows = shard_rows(w.n, world, rank, splits)
@@ -628,7 +629,6 @@ def refit_split(torch, dist, program, w, values, offsets, out, offsets_host, wor
     current split, fit the end weight to the ranks' times
     (sharding.fit_end_weight) and return (weight, fit, new split).  Every
     rank computes the same fit from the all-gathered times."""
-    from ragged.sharding import balanced_split, fit_end_weight, window_ends
     import statistics as st
     local = lambda edges: edges.repeat(world)  # same shape as the gathered records
     times = []
@@ -644,8 +644,16 @@ def refit_split(torch, dist, program, w, values, offsets, out, offsets_host, wor
     mine = torch.tensor([st.median(times)], dtype=torch.float64, device=values.device)
     every = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(every, mine)
-    rank_ms = [float(t.item()) for t in every]
-    rows = [shard_rows(w.n, world, r, splits)[1] - shard_rows(w.n, world, r, splits)[0] for r in range(world)]
+    return split_from_rank_times(w.n, offsets_host, world, splits, [float(t.item()) for t in every], weight)
+
+
+def split_from_rank_times(n, offsets_host, world, splits, rank_ms, weight):
+    """The host half of ``refit_split``: rows and segment ends of each
+    rank's window under ``splits``, the end weight fitted to the measured
+    per-rank times (``weight`` kept when the fit is not possible), and the
+    balanced split for it."""
+    from ragged.sharding import balanced_split, fit_end_weight, shard_rows, window_ends
+    rows = [shard_rows(n, world, r, splits)[1] - shard_rows(n, world, r, splits)[0] for r in range(world)]
     ends = window_ends(offsets_host, world, splits)
     fitted, info = fit_end_weight(rows, ends, rank_ms, weight)
     info = {**info, "model_weight": round(weight, 4), "fitted_weight": round(fitted, 4),

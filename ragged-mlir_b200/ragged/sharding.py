@@ -61,9 +61,13 @@ def window_ends(offsets: np.ndarray, world: int, splits) -> list[int]:
 
 def fit_end_weight(rows, ends, times_ms, fallback: float) -> tuple[float, dict]:
     """End weight from measured per-rank times of the local phase: the
-    least-squares fit t = c + a * rows + e * ends over the ranks (a, e >= 0),
-    weight e / a.  Needs at least four ranks with different mixes of rows
-    and ends; otherwise ``fallback`` is returned."""
+    least-squares fit t = a * rows + e * ends over the ranks (a, e >= 0),
+    weight e / a.  No fixed term: under a split that already balances
+    rows + w * ends, the ranks' rows and ends lie on a line, and a fixed
+    term would make the weight unidentifiable (a rank's fixed cost, a few
+    launches, is about 1 % of a c5 window's time).  Needs at least four ranks
+    with different mixes of rows and ends; otherwise ``fallback`` is
+    returned."""
     rows = np.asarray(rows, dtype=np.float64)
     ends = np.asarray(ends, dtype=np.float64)
     times = np.asarray(times_ms, dtype=np.float64)
@@ -71,14 +75,13 @@ def fit_end_weight(rows, ends, times_ms, fallback: float) -> tuple[float, dict]:
     if len(times) < 4 or np.ptp(ends) == 0 or np.ptp(rows) == 0:
         return fallback, {**info, "fit": "not enough distinct ranks; model weight kept"}
     from scipy.optimize import nnls
-    a = np.stack([np.ones_like(rows), rows / 1e6, ends / 1e6], axis=1)
+    a = np.stack([rows / 1e6, ends / 1e6], axis=1)
     coef, residual = nnls(a, times)
-    if coef[1] <= 0:
+    if coef[0] <= 0:
         return fallback, {**info, "fit": "no per-row cost in the fit; model weight kept"}
-    weight = float(np.clip(coef[2] / coef[1], 0.0, 64.0))
-    return weight, {**info, "fit": "least squares over ranks", "ms_fixed": round(float(coef[0]), 4),
-                    "ms_per_mrow": round(float(coef[1]), 5), "ms_per_mend": round(float(coef[2]), 5),
-                    "residual_ms": round(float(residual), 5)}
+    weight = float(np.clip(coef[1] / coef[0], 0.0, 64.0))
+    return weight, {**info, "fit": "least squares over ranks", "ms_per_mrow": round(float(coef[0]), 5),
+                    "ms_per_mend": round(float(coef[1]), 5), "residual_ms": round(float(residual), 5)}
 
 
 def shard_rows(n: int, world: int, rank: int, splits=None) -> tuple[int, int]:

@@ -79,3 +79,27 @@ def test_only_rank_zero_runs_the_reference_arm():
                        "200", "--warmup", "3", env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert result.returncode == 0, result.stderr[-2000:]
     assert result.stdout.strip() == ""
+
+
+def test_split_refit_from_rank_times():
+    """The sharded bench's split refit (world >= 4), host half: rank times
+    generated with a known end weight give that weight back, and the new
+    split balances rows + weight x ends; too few ranks keep the model weight."""
+    sys.path.insert(0, str(REPO))
+    import numpy as np
+    import bench
+    from ragged import workloads
+    from ragged.sharding import balanced_split, shard_rows, window_ends
+    w = workloads.make("c5", scale=0.001)
+    offsets = w.offsets().astype(np.int64)
+    world = 8
+    splits = balanced_split(offsets, world, 1.0)
+    rows = [shard_rows(w.n, world, r, splits)[1] - shard_rows(w.n, world, r, splits)[0] for r in range(world)]
+    ends = window_ends(offsets, world, splits)
+    true_weight = 6.0
+    times = [1e-6 * (r + true_weight * e) for r, e in zip(rows, ends)]
+    fitted, info, new_splits = bench.split_from_rank_times(w.n, offsets, world, splits, times, 1.25)
+    assert abs(fitted - true_weight) < 0.05 * true_weight, info
+    assert list(new_splits) == list(balanced_split(offsets, world, fitted))
+    kept, info, _ = bench.split_from_rank_times(w.n, offsets, 2, None, times[:2], 1.25)
+    assert kept == 1.25 and "kept" in info["fit"]
