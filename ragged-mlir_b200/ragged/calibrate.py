@@ -129,7 +129,15 @@ def measure(args: argparse.Namespace) -> None:
             "protocol": "median of 5 complete calls after 2 warm-up, CUDA events; L2 flushed when inputs < 4x L2",
             "cases": results}
     Path(args.output).parent.mkdir(parents=True, exist_ok=True)
-    Path(args.output).write_text(json.dumps(data, indent=1))
+    Path(args.output).write_text(compact_runs(data))
+
+
+def compact_runs(data: dict) -> str:
+    """A measurement file as JSON with one case per line."""
+    head = json.dumps({k: v for k, v in data.items() if k != "cases"})[:-1]
+    cases = ",\n".join(json.dumps(case, separators=(",", ":")) for case in data["cases"])
+    return f'{head}, "cases": [\n{cases}\n]}}\n'
+
 
 
 def _terms(case: dict, l2_mib: float) -> tuple[float, ...]:
