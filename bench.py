@@ -78,8 +78,8 @@ def parse_args(argv=None):
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-configs", action="store_true", help="skip the c1-c4 entries (N=1)")
     parser.add_argument("--no-parity", action="store_true", help="skip the oracle check of the first call")
-    parser.add_argument("--no-split-fit", action="store_true",
-                        help="keep the model end weight instead of refitting the split from measured rank times")
+    parser.add_argument("--split-fit", action="store_true",
+                        help="refit the split's end weight from measured per-rank times before timing (N > 1)")
     parser.add_argument("--cpu-bytes", type=float, default=2e9,
                         help="algorithmic bytes of the CPU sample (one call of each CPU implementation)")
     return parser.parse_args(argv)
@@ -483,10 +483,13 @@ def ours(args) -> None:
     flush = (lambda: flush_l2(flush_buffer)) if flush_buffer is not None else None
     report_holder = {}
     exchange = torch_exchange() if world > 1 else None
-    if world > 1 and not args.no_split_fit:
+    if world > 1 and args.split_fit:
         # Refit the split from measured local phases (the shard kernel and its
         # fix-up on each rank's rows, exchange left out), then re-shard (the
         # fit needs four ranks or more; with fewer the model weight stays).
+        # Off by default: calls timed one at a time after a host
+        # synchronisation run well above the back-to-back step time, which
+        # skews the fit.
         end_weight, split_fit, splits = refit_split(torch, dist, program, w, values, offsets, out, offsets_host,
                                                     world, rank, splits, end_weight)
         new_rows = shard_rows(w.n, world, rank, splits)
