@@ -401,7 +401,7 @@ def parity_sharded(torch, dist, w, values, out, offsets_host, row0, rank, world,
     """The first call's output over all ranks: each rank reduces its rows of
     the checked segments in the oracle; rank 0 merges the float64 pieces in
     rank order (the oracle's own merge) and compares the rows the owners
-    wrote.  Every rank takes the same collectives; the verdict is shared."""
+    wrote.  Every rank takes the same collectives; the outcome is shared."""
     from oracle import device_check as dc, native  # the checker
     segments = parity_segments(offsets_host)
     kinds = (w.op, "abssum") if w.op == "sum" else (w.op,)
@@ -414,7 +414,7 @@ def parity_sharded(torch, dist, w, values, out, offsets_host, row0, rank, world,
     rows_mine = out.index_select(0, torch.from_numpy(segments).to(device)).float()
     rows_every = [torch.empty_like(rows_mine) for _ in range(world)]
     dist.all_gather(rows_every, rows_mine)
-    verdict = torch.zeros(1, dtype=torch.int32, device=device)
+    failed = torch.zeros(1, dtype=torch.int32, device=device)
     message = ""
     if rank == 0:
         pieces = [e.cpu().numpy() for e in every]
@@ -430,10 +430,10 @@ def parity_sharded(torch, dist, w, values, out, offsets_host, row0, rank, world,
             native.check(actual, w.op, w.dtype, np.concatenate([[0], np.cumsum(lengths)]), merged[0],
                          merged[1] if w.op == "sum" else None)
         except AssertionError as exc:
-            verdict.fill_(1)
+            failed.fill_(1)
             message = str(exc)
-    dist.all_reduce(verdict, op=dist.ReduceOp.MAX)
-    if int(verdict.item()):
+    dist.all_reduce(failed, op=dist.ReduceOp.MAX)
+    if int(failed.item()):
         raise SystemExit(f"parity check of the first call failed: {message or 'see rank 0'}")
     rows = int(np.sum(np.diff(offsets_host.astype(np.int64))[segments]))
     return {"parity": "ok", "parity_segments": int(segments.size), "parity_rows": rows}
