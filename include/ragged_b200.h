@@ -264,6 +264,20 @@ int rg_shard_softmax_finish(int dtype, int index_dtype, int64_t d, int64_t n, in
 int rg_run_noalloc(int op, int dtype, int index_dtype, int64_t d, int64_t n, int64_t b,
                    const void *values, const void *offsets, void *out, uint32_t flags, void *stream);
 
+/* ------------------------------------------------------- schedule choice
+ * This build's extension (the reference chooses in Python,
+ * python/ragged/selection.py:106-126): the scores of the boosted decision
+ * trees that ragged/selection.py's TreeChooser stores as flat node arrays.
+ * Node i tests x[feature[i]] <= threshold[i] (then left[i], else right[i])
+ * unless leaf[i] != 0, where it holds value[i]; scores[c] = baseline[c] plus
+ * the leaf values reached in the trees whose tree_class is c.  Host memory
+ * only, no device needed.  RG_ERR_INVALID_ARGUMENT for an index out of range
+ * or a walk longer than max_depth. */
+int rg_tree_scores(int64_t nodes, const int32_t *feature, const double *threshold, const int32_t *left,
+                   const int32_t *right, const double *value, const uint8_t *leaf, int64_t trees,
+                   const int32_t *roots, const int32_t *tree_class, int classes, const double *baseline,
+                   int features, const double *x, int max_depth, double *scores);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -34,7 +34,7 @@ EXPORTED = ("rg_version", "rg_error_string", "rg_last_error", "rg_get_device_inf
             "rg_run", "rg_kernel_name", "rg_check_offsets", "rg_pointwise_workspace_bytes", "rg_run_pointwise",
             "rg_shard_rows", "rg_shard_split", "rg_shard_edge_bytes", "rg_shard_workspace_bytes",
             "rg_shard_segments", "rg_shard_softmax_workspace_bytes", "rg_run_shard_softmax",
-            "rg_shard_softmax_finish", "rg_run_shard", "rg_shard_combine", "rg_run_noalloc")
+            "rg_shard_softmax_finish", "rg_run_shard", "rg_shard_combine", "rg_run_noalloc", "rg_tree_scores")
 
 
 class Report(ctypes.Structure):
@@ -94,6 +94,8 @@ def library(path: Path | None = None):
         lib.rg_run_pointwise.restype = i32
         lib.rg_run_noalloc.argtypes = [i32, i32, i32, i64, i64, i64, p, p, p, u32, p]
         lib.rg_run_noalloc.restype = i32
+        lib.rg_tree_scores.argtypes = [i64, p, p, p, p, p, p, i64, p, p, i32, p, i32, p, i32, p]
+        lib.rg_tree_scores.restype = i32
         pi64 = ctypes.POINTER(i64)
         lib.rg_shard_rows.argtypes = [i64, i32, i32, pi64, pi64]
         lib.rg_shard_rows.restype = i32
@@ -324,3 +326,24 @@ def check_offsets(index: str, n: int, b: int, offsets_ptr: int, min_len: int | N
                                          -1 if max_len is None else max_len, status_ptr, stream or None,
                                          ctypes.byref(report)), "rg_check_offsets")
     return report
+
+
+def tree_scores(arrays: dict, x, classes: int, max_depth: int):
+    """Scores of the schedule chooser's trees (rg_tree_scores); ``arrays``
+    holds contiguous int32 feature/left/right/roots/tree_class, float64
+    threshold/value/baseline and uint8 leaf node arrays (kept alive by the
+    caller; their addresses are cached in it under "_args")."""
+    import numpy as np
+    lib = library()
+    args = arrays.get("_args")
+    if args is None:
+        a = arrays
+        args = arrays["_args"] = (a["feature"].size, a["feature"].ctypes.data, a["threshold"].ctypes.data,
+                                  a["left"].ctypes.data, a["right"].ctypes.data, a["value"].ctypes.data,
+                                  a["leaf"].ctypes.data, a["roots"].size, a["roots"].ctypes.data,
+                                  a["tree_class"].ctypes.data, classes, a["baseline"].ctypes.data)
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    scores = np.empty(classes, dtype=np.float64)
+    status = lib.rg_tree_scores(*args, x.size, x.ctypes.data, max_depth, scores.ctypes.data)
+    raise_for(status, "rg_tree_scores")
+    return scores

@@ -33,6 +33,7 @@ the stored margin.
 from __future__ import annotations
 
 from dataclasses import dataclass
+from functools import cached_property
 import json
 import math
 from pathlib import Path
@@ -144,6 +145,28 @@ class TreeChooser:
                 raise CacheMismatch("tree chooser does not reproduce its recorded choices")
         return chooser
 
+    @cached_property
+    def native_arrays(self) -> dict:
+        """The node arrays in the layout rg_tree_scores reads."""
+        i32 = lambda a: np.ascontiguousarray(a, dtype=np.int32)
+        f64 = lambda a: np.ascontiguousarray(a, dtype=np.float64)
+        return {"feature": i32(self.feature), "threshold": f64(self.threshold), "left": i32(self.left),
+                "right": i32(self.right), "value": f64(self.value), "leaf": np.ascontiguousarray(self.leaf, np.uint8),
+                "roots": i32(self.roots), "tree_class": i32(self.tree_class), "baseline": f64(self.baseline)}
+
+    def fast_scores(self, x: np.ndarray) -> np.ndarray:
+        """``scores`` computed by libragged_b200 (one walk per tree in C, a few
+        microseconds); the NumPy walk where the library cannot be loaded
+        (fitting a model on a machine without the build).  Both make the
+        same comparisons in float64."""
+        from . import _native
+        from .errors import RuntimeUnavailable
+        try:
+            _native.library()
+        except RuntimeUnavailable:
+            return self.scores(x)
+        return _native.tree_scores(self.native_arrays, x, len(self.classes), self.max_depth)
+
     def scores(self, x: np.ndarray) -> np.ndarray:
         node = self.roots.copy()
         for _ in range(self.max_depth + 1):
@@ -214,7 +237,7 @@ class CostModel:
                    "predicted_us": {s: round(v, 2) for s, v in predicted.items()}}
         ranked = [s for s in candidates if self.chooser is not None and s in self.chooser.classes]
         if ranked:
-            scores = self.chooser.scores(choice_features(op, n, b, d, max_len, element_bytes))
+            scores = self.chooser.fast_scores(choice_features(op, n, b, d, max_len, element_bytes))
             score = {s: float(scores[self.chooser.classes.index(s)]) for s in ranked}
             details["scores"] = {s: round(v, 4) for s, v in score.items()}
             return max(ranked, key=lambda s: (score[s], s == default)), details

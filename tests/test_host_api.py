@@ -161,6 +161,27 @@ def _chooser_dict(**overrides):
     return data
 
 
+def test_tree_scores_in_the_library_match_the_numpy_walk():
+    """rg_tree_scores (C, used by choose) and TreeChooser.scores (NumPy) give
+    identical scores for the shipped model on calibration cases, and the C
+    walk rejects out-of-range nodes instead of reading past the arrays."""
+    import json
+    from ragged import _native
+    from ragged.errors import ValidationError
+    model = selection.default_model()
+    chooser = model.chooser
+    data = json.loads((Path(selection.__file__).parent / "calibration" / "b200.json").read_text())
+    for case in data["cases"][::37]:
+        x = selection.choice_features(case["op"], case["n"], case["b"], case["d"], case["max_len"],
+                                      4 if case["dtype"] == "f32" else 2)
+        assert np.array_equal(chooser.fast_scores(x), chooser.scores(x))
+    toy = selection.TreeChooser.from_dict(_chooser_dict())
+    broken = {k: v for k, v in toy.native_arrays.items() if k != "_args"}
+    broken["left"] = np.array([-1, 9, -1, -1, -1], dtype=np.int32)
+    with pytest.raises(ValidationError, match="out of range"):
+        _native.tree_scores(broken, selection.choice_features("sum", 512, 4, 8, 128, 4), 3, toy.max_depth)
+
+
 def test_tree_chooser_choice_and_validation():
     linear = {"reduce": {s: [10, 0, 0, 0, 0, 0] for s in ("classified", "naive", "rowbalanced")},
               "softmax": {s: [10, 0, 0, 0, 0, 0] for s in ("classified", "naive")}}
