@@ -72,3 +72,28 @@ def test_tree_chooser_fit_reproduces_its_labels():
     model = CostModel(fitted, 0.0, {}, 126.0, chooser)
     hits, total, misses = calibrate.within_share(model, heldout, 126.0)
     assert hits >= 0.95 * total, misses
+
+
+def test_shipped_model_reproduces_its_recorded_held_out_share():
+    """The shipped cost model, evaluated on the shipped B200 measurements,
+    gives exactly the held-out share its calibration entry records (and
+    that share is at least 90 %)."""
+    import json
+    from pathlib import Path
+    from ragged import selection
+    model = selection.default_model()
+    data = json.loads((Path(selection.__file__).parent / "calibration" / "b200.json").read_text())
+    heldout = [c for c in data["cases"] if c["group"] == "heldout"]
+    hits, total, _ = calibrate.within_share(model, heldout, float(data["l2_mib"]))
+    assert total == model.calibration["heldout_cases"]
+    assert hits == model.calibration["heldout_within_3pct"]
+    assert hits >= 0.9 * total
+
+
+def test_measurement_files_are_one_case_per_line():
+    import json
+    data = {"device": "x", "l2_mib": 1.0, "protocol": "p",
+            "cases": [{"id": 0, "times_us": {"naive": 1.5}}, {"id": 1, "times_us": {"naive": 2.0}}]}
+    text = calibrate.compact_runs(data)
+    assert json.loads(text) == data
+    assert len(text.strip().splitlines()) == 4
